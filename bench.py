@@ -1,0 +1,520 @@
+#!/usr/bin/env python
+"""Benchmark of the Origami KV layout hot path on B200.
+
+Headline (N=1): config C2 restore — Llama-3-8B-shaped KV (32 layers, 8 KV heads, head_dim
+128, bf16, block 16), one request of 32768 tokens under a seeded block-table permutation.
+A step restores every layer (unpack + plane merge + scatter into the paged cache) from
+packed chunks resident in HBM; `value` is KV GB/s (bytes of K and V written into the
+cache per second, whole job). Weak scaling at N GPUs: N requests, heads sharded by rank
+(8/N heads per rank), i.e. the same bytes per GPU and no collective on the data path.
+
+Extra keys: `pack` (the save side over the same layers), `roofline` (the restore
+kernel's algorithmic bytes per launch over its CUDA-event duration vs measured HBM
+copy bandwidth), `e2e` (the same restore through the public pipeline API from pinned
+host chunks, H2D copies inside the timed region), `cpu_baseline` (the CPU oracle
+restore on the host cores, rank 0 at N=1), `clocks`, `gpu_launches`.
+
+`--impl reference` times the CPU implementation of the path (the oracle port of the
+reference layout: the reference's own CPU packer is a stub) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+GB = 1e9
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("origami", "reference"), default="origami")
+    ap.add_argument("--planes", default="byte", help="byte | bit | bf16_bits | fp16_bits")
+    ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="bound on the CPU baseline sample")
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------------------------------
+# distributed plumbing
+# ----------------------------------------------------------------------------------------
+def init_dist(backend: str):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        if backend == "nccl":
+            torch.cuda.set_device(local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", local))
+        else:
+            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+    elif backend == "nccl":
+        torch.cuda.set_device(local)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int, device=None) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ----------------------------------------------------------------------------------------
+# clocks during the timed region
+# ----------------------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self._t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self._t = threading.Thread(target=self._read, daemon=True)
+        self._t.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons, power = [], [], set(), []
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for name, val in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"),
+                                 parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm), "power_w_max": max(power) if power else None}
+
+
+def measured_hbm_peak():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return 6650.0, "fallback"
+
+
+def profiled_traffic(kernel: str, workload: str):
+    """dram read+write bytes per launch from the committed ncu summary, if any."""
+    p = REPO / "profiles" / "traffic.txt"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        parts = line.split()
+        if len(parts) >= 3 and parts[0] == kernel and parts[1] == workload:
+            return int(parts[2])
+    return None
+
+
+# ----------------------------------------------------------------------------------------
+# workload
+# ----------------------------------------------------------------------------------------
+class Workload:
+    """C2 at weak scaling: `world` requests of 32768 tokens, heads sharded by rank."""
+
+    def __init__(self, rank: int, world: int, layers: int, planes_name: str, device):
+        import torch
+
+        from origami_b200 import LayerFormat, plane_spec, workloads
+        from origami_b200.layer import pack_layer
+
+        cfg = workloads.C2
+        if cfg.heads % world:
+            raise SystemExit(f"{cfg.heads} KV heads do not shard over {world} ranks")
+        self.cfg = cfg
+        self.layers = layers
+        self.heads = cfg.heads // world
+        self.head0 = rank * self.heads
+        self.requests = world
+        self.T = cfg.tokens[0]
+        self.bs = cfg.block_size
+        nb = self.T // self.bs
+        self.NB = nb * self.requests
+        self.planes = plane_spec(planes_name, cfg.dtype)
+        self.fmt = LayerFormat(self.T, self.heads, cfg.head_dim, self.planes)
+        pool = workloads.permuted_block_table(self.NB, self.NB, workloads.SEED)
+        self.block_ids = [pool[r * nb:(r + 1) * nb].to(device) for r in range(self.requests)]
+        self.caches, self.packed, self.orig = [], [], []
+        for layer in range(layers):
+            cache = torch.empty((2, self.NB, self.bs, self.heads, cfg.head_dim), dtype=cfg.dtype, device=device)
+            per_req = []
+            for r in range(self.requests):
+                kv = workloads.kv_values(self.T, cfg.heads, cfg.head_dim, cfg.dtype, seed=workloads.SEED + 1000 * layer + r,
+                                         v_std=cfg.v_std, device=device)[:, :, self.head0:self.head0 + self.heads]
+                workloads.scatter_into_cache(cache, kv.contiguous(), self.block_ids[r])
+                per_req.append(pack_layer(cache, self.block_ids[r], self.fmt))
+            self.orig.append(cache.clone())
+            self.caches.append(cache)
+            self.packed.append(per_req)
+        torch.cuda.synchronize()
+
+    @property
+    def units_per_step(self) -> int:
+        return self.layers * self.requests
+
+    @property
+    def kv_bytes_per_step(self) -> int:
+        return self.units_per_step * self.fmt.kv_bytes
+
+    @property
+    def packed_bytes_per_step(self) -> int:
+        return self.units_per_step * self.fmt.packed_bytes
+
+    def verify(self) -> bool:
+        import torch
+
+        return all(torch.equal(c.view(torch.int16), o.view(torch.int16)) for c, o in zip(self.caches, self.orig))
+
+
+def run_origami(args, rank, world, local):
+    import torch
+
+    from origami_b200.layer import pack_layer, restore_layer
+    from origami_b200.pipeline import RestorePipeline
+
+    device = torch.device("cuda", local)
+    wl = Workload(rank, world, args.layers, args.planes, device)
+    stream = torch.cuda.current_stream(device)
+    err = torch.zeros(1, dtype=torch.int32, device=device)
+
+    # the originals are kept; zero the caches so the timed restores rebuild them
+    for c in wl.caches:
+        c.zero_()
+
+    def restore_step(events=None):
+        for layer in range(wl.layers):
+            for r in range(wl.requests):
+                if events is not None:
+                    events.append((torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)))
+                    events[-1][0].record(stream)
+                restore_layer(wl.packed[layer][r], wl.fmt, wl.caches[layer], wl.block_ids[r], error_count=err)
+                if events is not None:
+                    events[-1][1].record(stream)
+
+    def pack_step(events=None):
+        for layer in range(wl.layers):
+            for r in range(wl.requests):
+                if events is not None:
+                    events.append((torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)))
+                    events[-1][0].record(stream)
+                pack_layer(wl.caches[layer], wl.block_ids[r], wl.fmt, out=wl.packed[layer][r], error_count=err)
+                if events is not None:
+                    events[-1][1].record(stream)
+
+    def timed(step_fn):
+        """Per-launch CUDA-event durations from an eager pass, then the step time from
+        CUDA-graph replays of the same step (no host launch overhead in `value`)."""
+        for _ in range(args.warmup):
+            step_fn()
+        torch.cuda.synchronize(device)
+        launch_events = []
+        step_fn(launch_events)
+        torch.cuda.synchronize(device)
+        launch_ms = statistics.mean(a.elapsed_time(b) for a, b in launch_events)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step_fn()
+        for _ in range(args.warmup):
+            graph.replay()
+        barrier(world)
+        torch.cuda.synchronize(device)
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        t1.record(stream)
+        torch.cuda.synchronize(device)
+        barrier(world)
+        ms = t0.elapsed_time(t1)
+        del graph
+        return max_over_ranks(ms, world, device), launch_ms, len(launch_events) * args.steps
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    restore_ms, restore_launch_ms, restore_launches = timed(restore_step)
+    clock_info = clocks.stop()
+    ok = wl.verify() and int(err.item()) == 0
+    pack_ms, pack_launch_ms, pack_launches = timed(pack_step)
+    ok = ok and wl.verify() and int(err.item()) == 0
+
+    steps = args.steps
+    total_kv = wl.kv_bytes_per_step * world * steps
+    value = total_kv / (restore_ms / 1e3) / GB
+    peak, peak_kind = measured_hbm_peak()
+    alg_restore = wl.fmt.packed_bytes + wl.fmt.kv_bytes
+    achieved = alg_restore / (restore_launch_ms / 1e3) / GB
+    achieved_pack = alg_restore / (pack_launch_ms / 1e3) / GB
+    workload_name = f"C2_restore_T{wl.T}_H{wl.heads}_D{wl.cfg.head_dim}_{wl.planes.name}"
+
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(args, wl, device, world)
+        ok = ok and e2e.pop("ok")
+
+    result = {
+        "metric": "KV restore GB/s (unpack + plane merge + paged scatter), whole job",
+        "value": round(value, 1),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(restore_ms / steps, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "u16 (bf16 bit patterns)",
+        "data": "synthetic (seeded N(0,1) x log-uniform channel scales, K outliers x20, V N(0,0.5))",
+        "config": {
+            "workload": "C2: Llama-3-8B-shaped KV restore, 32768-token request, seeded block-table permutation",
+            "layers": wl.layers, "tokens_per_request": wl.T, "requests": wl.requests, "kv_heads": wl.cfg.heads,
+            "heads_per_rank": wl.heads, "head_dim": wl.cfg.head_dim, "block_size": wl.bs, "cache_dtype": "bf16",
+            "planes": wl.planes.name, "chunk_bytes": 1 << 20, "parallelism": f"kv-head shard x{world}, no collective",
+            "l2": "inputs larger than L2 (%.1f GiB packed + %.1f GiB cache per rank per step)" % (
+                wl.packed_bytes_per_step / 2**30, wl.kv_bytes_per_step / 2**30),
+        },
+        "roofline": {
+            "kernel": "restore_tiles",
+            "bound": "hbm",
+            "achieved": round(achieved, 1),
+            "peak": peak,
+            "peak_kind": peak_kind,
+            "unit": "GB/s",
+            "frac": round(achieved / peak, 4),
+            "traffic": profiled_traffic("restore_tiles", workload_name),
+            "algorithmic_bytes_per_launch": alg_restore,
+            "launch_ms": round(restore_launch_ms, 5),
+        },
+        "pack": {
+            "metric": "KV pack GB/s (gather + plane split + bitpack), whole job",
+            "value": round(wl.kv_bytes_per_step * world * steps / (pack_ms / 1e3) / GB, 1),
+            "unit": "GB/s",
+            "ms_per_step": round(pack_ms / steps, 4),
+            "roofline": {"kernel": "pack_tiles", "bound": "hbm", "achieved": round(achieved_pack, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved_pack / peak, 4),
+                         "traffic": profiled_traffic("pack_tiles", workload_name)},
+        },
+        "gpu_launches": restore_launches,
+        "clocks": clock_info,
+        "verified": bool(ok),
+    }
+    if e2e is not None:
+        result["e2e"] = e2e
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(args, wl)
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    return 0 if ok else 1
+
+
+def run_e2e(args, wl, device, world):
+    """Restore from pinned host chunks through RestorePipeline; H2D inside the timed region."""
+    import torch
+
+    from origami_b200.pipeline import RestorePipeline
+
+    host = [[torch.empty((wl.fmt.packed_bytes,), dtype=torch.uint8, pin_memory=True) for _ in range(wl.requests)]
+            for _ in range(wl.layers)]
+    for layer in range(wl.layers):
+        for r in range(wl.requests):
+            host[layer][r].copy_(wl.packed[layer][r], non_blocking=True)
+    torch.cuda.synchronize(device)
+    for c in wl.caches:
+        c.zero_()
+    pipe = RestorePipeline(device, wl.fmt.packed_bytes, slots=3)
+    err = torch.zeros(1, dtype=torch.int32, device=device)
+    err_host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+
+    def step():
+        ev = None
+        for layer in range(wl.layers):
+            for r in range(wl.requests):
+                ev = pipe.enqueue(host[layer][r], wl.fmt, wl.caches[layer], wl.block_ids[r], error_count=err)
+        pipe.restore_stream.wait_event(ev)
+        with torch.cuda.stream(pipe.restore_stream):
+            err_host.copy_(err, non_blocking=True)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(device)
+    barrier(world)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(pipe.copy_stream)
+    launches0 = pipe.launches
+    for _ in range(args.steps):
+        step()
+    t1.record(pipe.restore_stream)
+    torch.cuda.synchronize(device)
+    barrier(world)
+    ms = max_over_ranks(t0.elapsed_time(t1), world, device)
+    ok = wl.verify() and int(err_host.item()) == 0
+    value = wl.kv_bytes_per_step * world * args.steps / (ms / 1e3) / GB
+    h2d = wl.packed_bytes_per_step
+    return {"value": round(value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
+            "ms_per_step": round(ms / args.steps, 3), "pcie_h2d_gbs": round(h2d * args.steps / (ms / 1e3) / GB, 2),
+            "gpu_launches": pipe.launches - launches0, "pipeline": "pinned host -> copy stream -> 3-slot ring -> "
+            "restore stream, per-layer events", "ok": ok}
+
+
+def cpu_baseline(args, wl):
+    """The CPU oracle restore of a bounded sample of C2 layers on the host cores."""
+    import numpy as np
+    import torch
+
+    sys.path.insert(0, str(REPO / "oracle"))
+    import oracle
+
+    threads = os.cpu_count() or 1
+    oracle.set_threads(threads)
+    packed = [wl.packed[layer][0].cpu().numpy() for layer in range(min(wl.layers, 8))]
+    ids = wl.block_ids[0].cpu().numpy()
+    cache = np.zeros((2, wl.NB, wl.bs, wl.heads, wl.cfg.head_dim), dtype=np.uint16)
+    done = 0
+    t0 = time.perf_counter()
+    while done < len(packed):
+        oracle.restore_layer(packed[done], wl.planes.shifts, wl.planes.bits, wl.fmt.specs, cache, 0, ids, wl.T)
+        done += 1
+        if time.perf_counter() - t0 > args.cpu_seconds:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": round(done * wl.fmt.kv_bytes / dt / GB, 3), "unit": "GB/s", "cores": oracle.max_threads(),
+            "kind": "port", "sample": f"{done} C2 layers x 1 request ({done * wl.fmt.kv_bytes / 2**20:.0f} MiB KV), "
+            f"oracle restore_layer, {dt:.1f} s"}
+
+
+def run_reference(args, rank, world):
+    """CPU implementation of the path on the host cores (rank 0 only)."""
+    if rank != 0:
+        return 0
+    import numpy as np
+
+    sys.path.insert(0, str(REPO / "oracle"))
+    import oracle
+    from origami_b200 import LayerFormat, plane_spec, workloads
+
+    cfg = workloads.C2
+    heads = cfg.heads // world
+    T, bs = cfg.tokens[0], cfg.block_size
+    nb = T // bs
+    planes = plane_spec(args.planes, cfg.dtype)
+    fmt = LayerFormat(T, heads, cfg.head_dim, planes)
+    threads = os.cpu_count() or 1
+    oracle.set_threads(threads)
+    ids = workloads.permuted_block_table(nb, nb, workloads.SEED).numpy()
+    import torch
+
+    kv = workloads.kv_values(T, cfg.heads, cfg.head_dim, cfg.dtype, seed=workloads.SEED, v_std=cfg.v_std)
+    cache = torch.zeros((2, nb, bs, heads, cfg.head_dim), dtype=cfg.dtype)
+    workloads.scatter_into_cache(cache, kv[:, :, :heads].contiguous(), torch.from_numpy(ids))
+    c16 = cache.view(torch.int16).numpy().view(np.uint16).copy()
+    packed, _ = oracle.pack_layer(c16, 0, ids, T, planes.shifts, planes.bits, fmt.specs)
+    dst = np.zeros_like(c16)
+    # one step = one layer of one request (a bounded sample of the C2 step)
+    for _ in range(args.warmup):
+        oracle.restore_layer(packed, planes.shifts, planes.bits, fmt.specs, dst, 0, ids, T)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.restore_layer(packed, planes.shifts, planes.bits, fmt.specs, dst, 0, ids, T)
+    dt = time.perf_counter() - t0
+    ok = bool(np.array_equal(dst, c16))
+    value = fmt.kv_bytes * args.steps / dt / GB
+    sample = f"1 C2 layer x 1 request per step ({fmt.kv_bytes / 2**20:.0f} MiB KV), {heads} heads"
+    line = {
+        "impl": "reference",
+        "metric": "KV restore GB/s (unpack + plane merge + paged scatter), whole job",
+        "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(dt * 1e3 / args.steps, 2), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u16 (bf16 bit patterns)", "data": "synthetic",
+        "config": {"workload": "C2: Llama-3-8B-shaped KV restore, 32768-token request (bounded CPU sample)",
+                   "planes": planes.name},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": oracle.max_threads(), "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "verified": ok,
+        "note": "the reference's CPU layout packer/unpacker is a stub (native_cpu.py:137-161); this is the "
+                "oracle restatement of its format, timed on the host cores",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        rank, world, _ = init_dist("gloo")
+        rc = run_reference(args, rank, world)
+    else:
+        rank, world, local = init_dist("nccl")
+        rc = run_origami(args, rank, world, local)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return rc
+
+
+if __name__ == "__main__":
+    sys.exit(main())

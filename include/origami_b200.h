@@ -1,0 +1,186 @@
+/*
+ * origami_b200 — C ABI of the B200 (sm_100a) KV layout hot path.
+ *
+ * The library moves one layer of a vLLM paged KV cache between the cache and the
+ * "codec-friendly" chunked layout that Origami hands to its host lossless codec:
+ *
+ *   save    : gather a request's blocks -> split every 16-bit element into planes
+ *             -> canonical head > channel > token order -> dense LSB-first bitpack
+ *             into chunks sized by the head/channel chunk planner;
+ *   restore : the exact inverse, scattering straight into the paged cache through
+ *             the block table.
+ *
+ * The canonical chunk format is the one defined by Origami's CUDA unpack kernel
+ * (csrc/origami/bitpack_layout_cuda.cu:70-128): a chunk spec row
+ * [head_start, head_end, channel_start, channel_end, token_start, token_end]
+ * covers symbols in head > channel > token order; symbol i of a chunk with
+ * `bits` bits per symbol occupies stream bits [i*bits, (i+1)*bits), bit k of the
+ * stream being bit (k % 8) of byte (k / 8); a chunk holds ceil(n*bits/8) bytes
+ * (bitpack_layout_cuda.cpp:183-185).
+ *
+ * Conventions (all entry points):
+ *   - plain pointers and sizes only; `d_` pointers are device memory, `h_` host;
+ *   - every launch goes to the caller's stream; nothing synchronises the device;
+ *   - the entry points allocate no device memory and are safe to call from
+ *     several host threads at once (no shared mutable state);
+ *   - return ORIGAMI_OK (0) or a negative ORIGAMI_ERR_*; origami_last_error()
+ *     returns a message for the calling thread's last failure;
+ *   - `d_error_count` (nullable) is a device uint32 that kernels increment for
+ *     every row they had to skip (block id outside the cache); the caller owns it.
+ */
+#ifndef ORIGAMI_B200_H
+#define ORIGAMI_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* origami_stream_t; /* identical to cudaStream_t */
+
+enum {
+  ORIGAMI_OK = 0,
+  ORIGAMI_ERR_INVALID = -1,     /* argument / table validation failed       */
+  ORIGAMI_ERR_UNSUPPORTED = -2, /* valid request outside what this build does */
+  ORIGAMI_ERR_CUDA = -3         /* a CUDA runtime call failed                */
+};
+
+/* Paged-cache layouts accepted for one layer's cache tensor. */
+enum {
+  ORIGAMI_KV_FIRST = 0,    /* [2, num_blocks, block_size, num_heads, head_dim] (FlashAttention NHD) */
+  ORIGAMI_BLOCKS_FIRST = 1 /* [num_blocks, 2, block_size, num_heads, head_dim]                     */
+};
+
+/* One layer of a paged KV cache (device memory, contiguous in the layout above). */
+typedef struct origami_paged_kv {
+  void* d_data;
+  int32_t layout;     /* ORIGAMI_KV_FIRST or ORIGAMI_BLOCKS_FIRST */
+  int32_t elem_bytes; /* 2 (bf16 / fp16); the plane split works on the raw 16 bits */
+  int64_t num_blocks;
+  int64_t block_size;
+  int64_t num_heads;
+  int64_t head_dim;
+} origami_paged_kv;
+
+/* Plane split of a 16-bit element: plane p holds (x >> shift[p]) & ((1 << bits[p]) - 1).
+ * The planes must cover bits 0..15 exactly once; every plane has 1..8 bits. */
+#define ORIGAMI_MAX_PLANES 8
+typedef struct origami_planes {
+  int32_t num_planes;
+  int32_t shift[ORIGAMI_MAX_PLANES];
+  int32_t bits[ORIGAMI_MAX_PLANES];
+} origami_planes;
+
+/* Chunk table of one layer in the plane format.
+ * The same `num_specs` specs (rows of 6 int64, the planner's output) apply to every
+ * component; component q = kv * num_planes + p (K planes first, then V planes) and
+ * chunk k = q * num_specs + s. offsets[k] is the byte offset of chunk k inside the
+ * layer's packed buffer, offsets[2 * num_planes * num_specs] the total byte count.
+ * Device copies feed the kernels; host copies are validated and size the launch. */
+typedef struct origami_chunk_table {
+  const int64_t* d_specs;
+  const int64_t* d_offsets;
+  const int64_t* h_specs;
+  const int64_t* h_offsets;
+  int64_t num_specs;
+} origami_chunk_table;
+
+/* ---------------------------------------------------------------------------------
+ * Library
+ * ------------------------------------------------------------------------------- */
+int32_t origami_b200_version(void);
+const char* origami_last_error(void);
+/* Packed bytes of a chunk of `symbols` symbols at `bits` bits
+ * (replaces packed_bytes_for_symbols, bitpack_layout_cuda.cpp:183-185). */
+int64_t origami_packed_bytes(int64_t symbols, int32_t bits);
+
+/* ---------------------------------------------------------------------------------
+ * Canonical chunk ops on uint8 symbol tensors
+ * ------------------------------------------------------------------------------- */
+
+/* Drop-in for unpack_canonical_storage_chunks_cuda (bitpack_layout_cuda.cpp:316-400,
+ * bound at cpp:894-903, called by lossless/native_gpu.py:113-146).
+ * Same arguments and checks: flat_chunks holds every chunk back to back; offsets has
+ * num_chunks + 1 entries; bits_per_chunk 1..8; chunk_specs [num_chunks][6]; source
+ * shape of rank 3 or 4; axis_positions = {token, head, head_dim, layer or -1}.
+ * Writes the symbols into d_output (prod(shape) bytes, source layout); positions no
+ * chunk covers are zero, as in the reference. Tables are passed both on the device
+ * (read by the kernels) and on the host (validated, no device->host copies). */
+int32_t origami_unpack_canonical_storage_chunks(
+    const uint8_t* d_flat_chunks, int64_t flat_bytes,
+    const int64_t* d_chunk_offsets, const int64_t* d_bits_per_chunk,
+    const int64_t* d_chunk_specs, const int64_t* h_chunk_offsets,
+    const int64_t* h_bits_per_chunk, const int64_t* h_chunk_specs,
+    int64_t num_chunks, const int64_t* h_source_shape, int32_t source_rank,
+    const int64_t* h_axis_positions, int64_t token_count, int64_t num_heads,
+    int64_t head_dim, uint8_t* d_output, int64_t output_bytes,
+    origami_stream_t stream);
+
+/* Inverse of the above, replacing the stub pack_canonical_storage_chunks
+ * (lossless/native_cpu.py:144-151; called by worker.py:2010-2016). Symbols are
+ * masked to `bits`; pad bits of a chunk's last byte are zero. d_flat_chunks must be
+ * 16-byte aligned and hold offsets[num_chunks] bytes; chunks must not overlap. */
+int32_t origami_pack_canonical_storage_chunks(
+    const uint8_t* d_symbols, int64_t symbol_bytes,
+    const int64_t* d_chunk_offsets, const int64_t* d_bits_per_chunk,
+    const int64_t* d_chunk_specs, const int64_t* h_chunk_offsets,
+    const int64_t* h_bits_per_chunk, const int64_t* h_chunk_specs,
+    int64_t num_chunks, const int64_t* h_source_shape, int32_t source_rank,
+    const int64_t* h_axis_positions, int64_t token_count, int64_t num_heads,
+    int64_t head_dim, uint8_t* d_flat_chunks, int64_t flat_bytes,
+    origami_stream_t stream);
+
+/* ---------------------------------------------------------------------------------
+ * Fused layer ops on the paged cache (plane format)
+ * ------------------------------------------------------------------------------- */
+
+/* Save side of one layer: gather the first num_tokens tokens of a request through
+ * d_block_ids[ceil(num_tokens / block_size)] (int64), split K and V into planes and
+ * pack every component in canonical order into d_packed (16-byte aligned,
+ * h_offsets[last] bytes). Replaces _select_blocks + quantize + _pack_quantized_symbols
+ * (worker.py:1887-1897, 1899-2040). The chunk specs must have token range
+ * [0, num_tokens) and partition (head, channel) of the cache's heads. */
+int32_t origami_pack_layer_from_paged(
+    const origami_paged_kv* cache, const int64_t* d_block_ids,
+    int64_t num_block_ids, int64_t num_tokens, const origami_planes* planes,
+    const origami_chunk_table* table, uint8_t* d_packed, int64_t packed_bytes,
+    uint32_t* d_error_count, origami_stream_t stream);
+
+/* Restore side of one layer: unpack every component, merge the planes and scatter
+ * tokens [0, num_tokens) into the paged cache through d_block_ids. Slots of the last
+ * block past num_tokens are left untouched. Replaces the GPU bit-unpack + dequantize +
+ * copy_kv_to_hbm of worker.py:1087-1248 (native_gpu.py:113-146,
+ * benchmark_utils.py:434-532). */
+int32_t origami_restore_layer_to_paged(
+    const uint8_t* d_packed, int64_t packed_bytes, const origami_planes* planes,
+    const origami_chunk_table* table, const origami_paged_kv* cache,
+    const int64_t* d_block_ids, int64_t num_block_ids, int64_t num_tokens,
+    uint32_t* d_error_count, origami_stream_t stream);
+
+/* ---------------------------------------------------------------------------------
+ * Raw-bytes path (the reference's lossless RawBytesTensorAdapter layout)
+ * ------------------------------------------------------------------------------- */
+
+/* index_select of d_block_ids[num_block_ids] along the cache's block dimension into
+ * d_out ([2, n, bs, H, D] for KV_FIRST, [n, 2, bs, H, D] for BLOCKS_FIRST); the bytes
+ * of d_out are the reference's raw-bytes symbols, i.e. the concatenation of its
+ * 1 MiB chunks (worker.py:1881-1897, quantization/raw_tensor.py:100-122). */
+int32_t origami_gather_blocks(const origami_paged_kv* cache,
+                              const int64_t* d_block_ids, int64_t num_block_ids,
+                              void* d_out, int64_t out_bytes,
+                              uint32_t* d_error_count, origami_stream_t stream);
+
+/* index_copy_ of d_in (layout as above) into the cache's blocks
+ * (benchmark_utils.py:434-444). */
+int32_t origami_scatter_blocks(const void* d_in, int64_t in_bytes,
+                               const origami_paged_kv* cache,
+                               const int64_t* d_block_ids, int64_t num_block_ids,
+                               uint32_t* d_error_count, origami_stream_t stream);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* ORIGAMI_B200_H */

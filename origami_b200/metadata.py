@@ -1,0 +1,46 @@
+"""Chunk-table records of the Origami artifact.
+
+Field-for-field the records of the reference connector (metadata.py:22-61 in the
+reference's origami package), so payloads written by either side stay interchangeable.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Any
+
+import torch
+
+
+@dataclass(frozen=True)
+class ChunkLayout:
+    layer_index: int
+    head_start: int
+    head_end: int
+    channel_start: int
+    channel_end: int
+    token_start: int
+    token_end: int
+    unpacked_bytes: int
+
+    def spec(self) -> list[int]:
+        """The [h0, h1, c0, c1, t0, t1] spec row of this chunk (worker.py:2207-2216)."""
+        return [self.head_start, self.head_end, self.channel_start, self.channel_end,
+                self.token_start, self.token_end]
+
+
+@dataclass
+class ChunkRecord:
+    chunk_id: int
+    layout: ChunkLayout
+    codec: str
+    compressed: torch.Tensor
+    compressed_bytes: int
+    unpacked_bytes: int
+
+
+@dataclass
+class LayerPayload:
+    layer_name: str
+    quantizer: str
+    quant_metadata: dict[str, Any]
+    chunks: list[ChunkRecord] = field(default_factory=list)

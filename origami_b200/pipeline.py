@@ -1,0 +1,118 @@
+"""Layer-wise restore / save pipelines around the fused kernels.
+
+RestorePipeline: packed layers live in pinned host memory (where the host codec
+decompresses them). Each enqueued layer is copied host->device on a dedicated copy
+stream into one slot of a small device ring (3 slots, the reference's
+qat_pipeline_slots default, config.py:73), unpacked and scattered into the paged cache
+on a restore stream that waits only for its own copy, and marked with a per-layer CUDA
+event. The H2D copy of layer L+1 therefore overlaps the unpack/scatter of layer L and
+whatever the model runs on its compute stream. ``wait_for_layer_load`` is a
+stream->event wait, never a host block (the reference blocks on a future and then waits,
+worker.py:553-572).
+
+SavePipeline: the mirror image: pack each layer on a save stream into a device slot
+and copy it to pinned host memory on a copy stream, one event per layer for the host
+codec to wait on.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from origami_b200.layer import pack_layer, restore_layer
+from origami_b200.planes import LayerFormat
+
+
+@dataclass
+class _Slot:
+    buf: torch.Tensor
+    copied: torch.cuda.Event
+    free: torch.cuda.Event
+    used: bool = False
+
+
+class RestorePipeline:
+    def __init__(self, device: torch.device, slot_bytes: int, slots: int = 3, *, priority: int = 0):
+        self.device = torch.device(device)
+        self.copy_stream = torch.cuda.Stream(self.device, priority=priority)
+        self.restore_stream = torch.cuda.Stream(self.device, priority=priority)
+        n = (int(slot_bytes) + 15) // 16 * 16
+        self.slots = [_Slot(torch.empty((n,), dtype=torch.uint8, device=self.device), torch.cuda.Event(),
+                            torch.cuda.Event()) for _ in range(max(1, slots))]
+        self._next = 0
+        self.launches = 0
+
+    def enqueue(self, host_packed: torch.Tensor, fmt: LayerFormat, kv_layer: torch.Tensor, block_ids,
+                error_count: torch.Tensor | None = None) -> torch.cuda.Event:
+        """Queue one layer; returns the event that marks the layer as restored."""
+        if host_packed.device.type != "cpu" or not host_packed.is_pinned():
+            raise ValueError("host packed layer must be in pinned host memory")
+        n = fmt.packed_bytes
+        if host_packed.numel() < n:
+            raise ValueError("host packed layer is shorter than the layer format")
+        slot = self.slots[self._next]
+        self._next = (self._next + 1) % len(self.slots)
+        if slot.buf.numel() < n:
+            raise ValueError("pipeline slot smaller than the packed layer")
+        if slot.used:
+            self.copy_stream.wait_event(slot.free)  # previous user of the slot has been unpacked
+        with torch.cuda.stream(self.copy_stream):
+            slot.buf[:n].copy_(host_packed[:n], non_blocking=True)
+            slot.copied.record(self.copy_stream)
+        self.restore_stream.wait_event(slot.copied)
+        restore_layer(slot.buf[:n], fmt, kv_layer, block_ids, stream=self.restore_stream, error_count=error_count)
+        self.launches += 1
+        slot.free.record(self.restore_stream)
+        slot.used = True
+        ready = torch.cuda.Event()
+        ready.record(self.restore_stream)
+        return ready
+
+    @staticmethod
+    def wait_for_layer_load(event: torch.cuda.Event, stream: torch.cuda.Stream | None = None) -> None:
+        (stream or torch.cuda.current_stream()).wait_event(event)
+
+    def synchronize(self) -> None:
+        self.copy_stream.synchronize()
+        self.restore_stream.synchronize()
+
+
+class SavePipeline:
+    def __init__(self, device: torch.device, slot_bytes: int, slots: int = 3):
+        self.device = torch.device(device)
+        self.save_stream = torch.cuda.Stream(self.device)
+        self.copy_stream = torch.cuda.Stream(self.device)
+        n = (int(slot_bytes) + 15) // 16 * 16
+        self.slots = [_Slot(torch.empty((n,), dtype=torch.uint8, device=self.device), torch.cuda.Event(),
+                            torch.cuda.Event()) for _ in range(max(1, slots))]
+        self._next = 0
+        self.launches = 0
+
+    def enqueue(self, kv_layer: torch.Tensor, block_ids, fmt: LayerFormat, host_out: torch.Tensor,
+                *, after: torch.cuda.Event | None = None,
+                error_count: torch.Tensor | None = None) -> torch.cuda.Event:
+        """Pack one layer into pinned `host_out`; returns the event after the D2H copy.
+
+        `after` (optional) is the event the layer's KV is complete at (e.g. recorded on
+        the model stream after attention wrote it)."""
+        if not host_out.is_pinned():
+            raise ValueError("host output must be pinned")
+        n = fmt.packed_bytes
+        slot = self.slots[self._next]
+        self._next = (self._next + 1) % len(self.slots)
+        if slot.used:
+            self.save_stream.wait_event(slot.free)
+        if after is not None:
+            self.save_stream.wait_event(after)
+        pack_layer(kv_layer, block_ids, fmt, out=slot.buf[:n], stream=self.save_stream, error_count=error_count)
+        self.launches += 1
+        slot.copied.record(self.save_stream)
+        self.copy_stream.wait_event(slot.copied)
+        with torch.cuda.stream(self.copy_stream):
+            host_out[:n].copy_(slot.buf[:n], non_blocking=True)
+        slot.free.record(self.copy_stream)
+        slot.used = True
+        done = torch.cuda.Event()
+        done.record(self.copy_stream)
+        return done

@@ -1,0 +1,137 @@
+"""Fused layer save / restore on the paged cache against the CPU oracle, plus the
+raw-bytes gather / scatter against torch's index_select / index_copy_."""
+import numpy as np
+import pytest
+import torch
+
+from origami_b200 import BF16_BIT_PLANES, BYTE_PLANES, FP16_BIT_PLANES, LayerFormat, PlaneSpec, workloads
+from origami_b200.layer import gather_blocks, pack_layer, restore_layer, scatter_blocks
+
+pytestmark = pytest.mark.gpu
+
+ODD_PLANES = PlaneSpec("odd", (12, 4, 0, 9), (4, 5, 4, 3))
+GEOMS = [
+    # T, block_size, heads, head_dim, chunk target bytes
+    (1024, 16, 8, 128, 1 << 20),
+    (1000, 16, 8, 128, 1 << 20),
+    (37, 16, 2, 64, 1 << 20),
+    (333, 32, 4, 256, 1 << 14),
+    (4096, 16, 2, 128, 1 << 16),
+    (8191, 16, 1, 128, 100_000),
+    (70, 16, 3, 8, 1 << 20),
+]
+PLANES = [BYTE_PLANES, BF16_BIT_PLANES, FP16_BIT_PLANES, ODD_PLANES]
+
+
+def make_cache(T, bs, H, D, kv_first, seed, dtype=torch.bfloat16, slack=3):
+    nb = (T + bs - 1) // bs
+    NB = nb + slack
+    ids = workloads.permuted_block_table(nb, NB, seed)
+    kv = workloads.kv_values(T, H, D, dtype, seed=seed)
+    shape = (2, NB, bs, H, D) if kv_first else (NB, 2, bs, H, D)
+    g = torch.Generator().manual_seed(seed + 99)
+    cache = torch.randint(-32768, 32767, shape, generator=g, dtype=torch.int16).view(dtype)
+    workloads.scatter_into_cache(cache, kv, ids, kv_first)
+    return cache, ids
+
+
+def u16(t):
+    return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+@pytest.mark.parametrize("kv_first", [True, False])
+@pytest.mark.parametrize("planes", PLANES, ids=lambda p: p.name)
+@pytest.mark.parametrize("geom", GEOMS, ids=lambda g: "T%d_bs%d_H%d_D%d" % g[:4])
+def test_pack_and_restore_match_oracle(oracle, cuda, geom, planes, kv_first):
+    T, bs, H, D, tgt = geom
+    layout = 0 if kv_first else 1
+    cache, ids = make_cache(T, bs, H, D, kv_first, seed=T + H + D)
+    fmt = LayerFormat(T, H, D, planes, tgt, tgt, tgt)
+    want, offsets = oracle.pack_layer(u16(cache), layout, ids.numpy(), T, planes.shifts, planes.bits, fmt.specs)
+    np.testing.assert_array_equal(offsets, fmt.offsets)
+    d_cache = cache.to(cuda)
+    out = fmt.alloc_packed(cuda)
+    out.fill_(0xA5)  # stale bytes must not leak into the result
+    got = pack_layer(d_cache, ids, fmt, out=out)
+    np.testing.assert_array_equal(got.cpu().numpy(), want)
+
+    # restore into a cache holding different bytes: only the request's token rows change
+    dst, _ = make_cache(T, bs, H, D, kv_first, seed=T + H + D + 1)
+    expect = u16(dst).copy()
+    oracle.restore_layer(want, planes.shifts, planes.bits, fmt.specs, expect, layout, ids.numpy(), T)
+    d_dst = dst.to(cuda)
+    restore_layer(torch.from_numpy(want).to(cuda), fmt, d_dst, ids.to(cuda))
+    np.testing.assert_array_equal(u16(d_dst.cpu()), expect)
+    # and the restored tokens are the saved tokens
+    back = workloads.tokens_from_cache(d_dst.cpu(), ids, T, kv_first)
+    orig = workloads.tokens_from_cache(cache, ids, T, kv_first)
+    assert torch.equal(back.view(torch.int16), orig.view(torch.int16))
+
+
+def test_fp16_cache_roundtrip(cuda):
+    T, bs, H, D = 777, 32, 8, 128
+    cache, ids = make_cache(T, bs, H, D, True, seed=5, dtype=torch.float16)
+    fmt = LayerFormat(T, H, D, FP16_BIT_PLANES)
+    d = cache.to(cuda)
+    packed = pack_layer(d, ids, fmt)
+    fresh = torch.zeros_like(d)
+    restore_layer(packed, fmt, fresh, ids)
+    t = torch.arange(T)
+    blk = ids[t // bs]
+    assert torch.equal(fresh.cpu()[:, blk, t % bs].view(torch.int16), cache[:, blk, t % bs].view(torch.int16))
+
+
+def test_bad_block_ids_are_counted_and_skipped(cuda):
+    T, bs, H, D = 64, 16, 2, 64
+    cache, ids = make_cache(T, bs, H, D, True, seed=11)
+    fmt = LayerFormat(T, H, D, BYTE_PLANES)
+    d = cache.to(cuda)
+    packed = pack_layer(d, ids, fmt)
+    bad = ids.clone()
+    bad[2] = 10_000
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    fresh = torch.zeros_like(d)
+    restore_layer(packed, fmt, fresh, bad, error_count=err)
+    assert int(err.item()) == 2 * H * bs  # every (kv, head, token) row of the bad block
+    good = [0, 1, 3]
+    t = torch.cat([torch.arange(b * bs, (b + 1) * bs) for b in good])
+    blk = ids[t // bs]
+    assert torch.equal(fresh.cpu()[:, blk, t % bs], cache[:, blk, t % bs])
+    err.zero_()
+    pack_layer(d, bad, fmt, error_count=err)
+    assert int(err.item()) > 0
+
+
+def test_c2_layer_roundtrip_full_size(cuda):
+    """One full C2 layer (32768 tokens, 8 heads): pack -> restore is the identity."""
+    cfg = workloads.C2
+    T = cfg.tokens[0]
+    nb = T // cfg.block_size
+    ids = workloads.permuted_block_table(nb, nb, workloads.SEED).to(cuda)
+    kv = workloads.kv_values(T, cfg.heads, cfg.head_dim, cfg.dtype, seed=workloads.SEED, v_std=cfg.v_std, device=cuda)
+    cache = torch.empty((2, nb, cfg.block_size, cfg.heads, cfg.head_dim), dtype=cfg.dtype, device=cuda)
+    workloads.scatter_into_cache(cache, kv, ids)
+    for planes in (BYTE_PLANES, BF16_BIT_PLANES):
+        fmt = LayerFormat(T, cfg.heads, cfg.head_dim, planes)
+        packed = pack_layer(cache, ids, fmt)
+        fresh = torch.zeros_like(cache)
+        restore_layer(packed, fmt, fresh, ids)
+        assert torch.equal(fresh.view(torch.int16), cache.view(torch.int16))
+        # plane 0 of K (exponent bits) is the first component; it must be far from uniform
+        hi = packed[: int(fmt.offsets[fmt.num_specs])].cpu().numpy()
+        assert len(np.unique(hi)) < 200
+
+
+@pytest.mark.parametrize("kv_first", [True, False])
+def test_raw_gather_scatter_match_torch(cuda, kv_first):
+    cache, ids = make_cache(500, 16, 4, 64, kv_first, seed=3, slack=9)
+    d = cache.to(cuda)
+    dim = 1 if kv_first else 0
+    got = gather_blocks(d, ids)
+    want = torch.index_select(d, dim, ids.to(cuda))
+    assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+    fresh = torch.zeros_like(d)
+    scatter_blocks(got, fresh, ids)
+    expect = torch.zeros_like(d)
+    expect.index_copy_(dim, ids.to(cuda), want)
+    assert torch.equal(fresh.view(torch.int16), expect.view(torch.int16))
