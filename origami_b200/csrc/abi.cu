@@ -116,24 +116,21 @@ bool covers_head_channel_exactly(const std::vector<Spec>& specs, int64_t H, int6
   return at == H * D;
 }
 
-int tile_tokens(int64_t D) { return static_cast<int>(8 * (2048 / D)); }
+int tile_tokens(int64_t D) { return origami::tile_tokens_for(static_cast<int>(D)); }
 
-// Shared-memory layout of a tile launch. Returns the dynamic smem byte count.
+// Shared-memory layout of a tile launch (must match the kernels' plane_stride /
+// plane_base). Returns the dynamic smem byte count.
 size_t layout_tile_smem(TileArgs& a, int elem, bool restore, const int* plane_bits) {
   const int D = a.D, TT = a.TT, P = a.P;
   size_t off = static_cast<size_t>((2 * D + 15) & ~15);
+  a.rowoff_off = static_cast<int32_t>(off);
+  off += static_cast<size_t>(8) * TT;
   a.meta_off = static_cast<int32_t>(off);
   off += static_cast<size_t>(16) * P * D;
   off = (off + 127) & ~static_cast<size_t>(127);
   a.data_off = static_cast<int32_t>(off);
   size_t planes_bytes = 0;
-  for (int p = 0; p < P; ++p) {
-    const int b = plane_bits[p];
-    const int run = ((TT * b + 7) / 8 + 15) & ~15;
-    a.rs[p] = restore ? run + 32 : run;
-    a.plane_base[p] = static_cast<int32_t>(planes_bytes);
-    planes_bytes += static_cast<size_t>(D) * a.rs[p];
-  }
+  for (int p = 0; p < P; ++p) planes_bytes += static_cast<size_t>(D) * origami::run_stride(TT, plane_bits[p], restore);
   const size_t rows_bytes = static_cast<size_t>(TT) * D * elem;
   return off + std::max(planes_bytes, rows_bytes);
 }
@@ -197,10 +194,10 @@ int32_t validate_cache(const origami_paged_kv* kv, PagedGeom& g) {
   return ORIGAMI_OK;
 }
 
-template <int ELEM, int MODE>
+template <int ELEM, int MODE, int DT>
 int32_t launch_tiles(bool restore, TileArgs& a, size_t smem, cudaStream_t st) {
-  const void* fn = restore ? reinterpret_cast<const void*>(&origami::restore_tiles<ELEM, MODE>)
-                           : reinterpret_cast<const void*>(&origami::pack_tiles<ELEM, MODE>);
+  const void* fn = restore ? reinterpret_cast<const void*>(&origami::restore_tiles<ELEM, MODE, DT>)
+                           : reinterpret_cast<const void*>(&origami::pack_tiles<ELEM, MODE, DT>);
   if (smem > 48 * 1024) {
     const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
@@ -209,18 +206,28 @@ int32_t launch_tiles(bool restore, TileArgs& a, size_t smem, cudaStream_t st) {
   if (tiles <= 0) return ORIGAMI_OK;
   if (tiles > 0x7FFFFFFF) return fail(ORIGAMI_ERR_UNSUPPORTED, "too many tiles");
   const dim3 grid(static_cast<unsigned>(tiles));
-  if (restore) origami::restore_tiles<ELEM, MODE><<<grid, kThreads, smem, st>>>(a);
-  else origami::pack_tiles<ELEM, MODE><<<grid, kThreads, smem, st>>>(a);
+  if (restore) origami::restore_tiles<ELEM, MODE, DT><<<grid, kThreads, smem, st>>>(a);
+  else origami::pack_tiles<ELEM, MODE, DT><<<grid, kThreads, smem, st>>>(a);
   return after_launch(restore ? "restore_tiles launch" : "pack_tiles launch");
 }
 
+template <int ELEM, int MODE>
+int32_t launch_by_dim(bool restore, TileArgs& a, size_t smem, cudaStream_t st) {
+  switch (a.D) {
+    case 64: return launch_tiles<ELEM, MODE, 64>(restore, a, smem, st);
+    case 128: return launch_tiles<ELEM, MODE, 128>(restore, a, smem, st);
+    case 256: return launch_tiles<ELEM, MODE, 256>(restore, a, smem, st);
+    default: return launch_tiles<ELEM, MODE, 0>(restore, a, smem, st);
+  }
+}
+
 int32_t dispatch_tiles(bool restore, int elem, int mode, TileArgs& a, size_t smem, cudaStream_t st) {
-  if (elem == 1) return launch_tiles<1, origami::kModeGeneric>(restore, a, smem, st);
+  if (elem == 1) return launch_by_dim<1, origami::kModeGeneric>(restore, a, smem, st);
   switch (mode) {
-    case origami::kModeByte2: return launch_tiles<2, origami::kModeByte2>(restore, a, smem, st);
-    case origami::kModeBf16Bits: return launch_tiles<2, origami::kModeBf16Bits>(restore, a, smem, st);
-    case origami::kModeFp16Bits: return launch_tiles<2, origami::kModeFp16Bits>(restore, a, smem, st);
-    default: return launch_tiles<2, origami::kModeGeneric>(restore, a, smem, st);
+    case origami::kModeByte2: return launch_by_dim<2, origami::kModeByte2>(restore, a, smem, st);
+    case origami::kModeBf16Bits: return launch_by_dim<2, origami::kModeBf16Bits>(restore, a, smem, st);
+    case origami::kModeFp16Bits: return launch_by_dim<2, origami::kModeFp16Bits>(restore, a, smem, st);
+    default: return launch_tiles<2, origami::kModeGeneric, 0>(restore, a, smem, st);
   }
 }
 
@@ -231,6 +238,7 @@ int32_t canonical_common(bool restore, const uint8_t* d_packed, int64_t packed_b
                          int64_t n, const int64_t* shape, int32_t rank, const int64_t* axes, int64_t T,
                          int64_t H, int64_t D, uint8_t* d_symbols, int64_t symbol_bytes, cudaStream_t st) {
   if (T <= 0 || H <= 0 || D <= 0) return fail(ORIGAMI_ERR_INVALID, "canonical symbol shape must be positive");
+  if (T > 0x7FFFFFFF) return fail(ORIGAMI_ERR_UNSUPPORTED, "token_count must be below 2^31");
   CanonStrides ls{};
   int64_t numel = 0;
   int32_t rc = read_layout(shape, rank, axes, T, H, D, ls, numel);
@@ -340,6 +348,8 @@ int32_t layer_common(bool restore, const origami_paged_kv* cache, const int64_t*
   if (D % 8 != 0 || D > 1024) return fail(ORIGAMI_ERR_UNSUPPORTED, "head_dim must be a multiple of 8, at most 1024");
   if (planes->num_planes * D > 2048) return fail(ORIGAMI_ERR_UNSUPPORTED, "num_planes * head_dim must be <= 2048");
   if (T <= 0) return fail(ORIGAMI_ERR_INVALID, "num_tokens must be positive");
+  if (T > 0x7FFFFFFF || cache->block_size > 0x7FFFFFFF)
+    return fail(ORIGAMI_ERR_UNSUPPORTED, "num_tokens and block_size must be below 2^31");
   const int64_t need_blocks = (T + cache->block_size - 1) / cache->block_size;
   if (d_block_ids == nullptr || num_block_ids < need_blocks)
     return fail(ORIGAMI_ERR_INVALID, "block table has %lld ids, %lld tokens need %lld", (long long)num_block_ids,

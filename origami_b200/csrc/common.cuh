@@ -11,6 +11,15 @@ constexpr int kThreads = 256;
 __host__ __device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
 __host__ __device__ __forceinline__ int64_t max64(int64_t a, int64_t b) { return a > b ? a : b; }
 
+// Tokens per tile for head_dim D: (TT/8) * (D/8) <= 256 work items of 8x8 elements.
+__host__ __device__ constexpr int tile_tokens_for(int D) { return 8 * (2048 / D); }
+
+// Shared-memory row stride of one (plane, channel) run of TT symbols at `bits` bits:
+// 16-byte rounded; restore rows get 32 spare bytes for unaligned run starts.
+__host__ __device__ constexpr int run_stride(int TT, int bits, bool restore) {
+  return ((((TT * bits + 7) / 8) + 15) & ~15) + (restore ? 32 : 0);
+}
+
 // ---------------------------------------------------------------------------
 // Asynchronous global -> shared copies (bypass registers, complete at wait).
 // ---------------------------------------------------------------------------

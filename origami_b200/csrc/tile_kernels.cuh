@@ -8,11 +8,16 @@
 // (paged KV cache rows, or a [.., head, head_dim]-innermost uint8 symbol tensor).
 //
 // restore_tiles: packed runs -(cp.async)-> smem rows [p][c][bits] -> 8x8 byte transposes
-//   in registers -> plane merge -> smem rows [t][c] (rotated 16-byte chunks, bank-conflict
-//   free) -> 16-byte streaming stores into the destination rows via the block table.
-// pack_tiles: the inverse; partially owned 32-bit words at run edges are merged with
-//   masked atomics so any bit alignment (ragged token counts, odd bit widths) is exact
-//   without a zero-fill pass.
+//   in registers -> plane merge -> smem rows [t][c] (16-byte chunks rotated by token octet,
+//   bank-conflict free) -> 16-byte streaming stores into the destination rows.
+// pack_tiles: the inverse. Fully owned, aligned 16-byte vectors of a run are stored
+//   whole; 32-bit words a run shares with its neighbour are merged with masked atomics,
+//   so any bit alignment (ragged token counts, odd bit widths) is exact without a
+//   zero-fill pass.
+//
+// Template parameters: ELEM (row element bytes: 2 = bf16/fp16 cache, 1 = uint8 symbols),
+// MODE (plane preset with compile-time shifts and widths, or generic), DT (head_dim when
+// it is 64/128/256 so every index division folds to shifts; 0 = runtime head_dim).
 #pragma once
 
 #include "common.cuh"
@@ -52,14 +57,12 @@ struct TileArgs {
   int32_t num_kv, H, D;
   int64_t T;
   int32_t TT, tiles_per_head;
-  // Planes.
+  // Planes (bits[p] is the widest chunk's width when chunk_bits is set).
   int32_t P;
   int32_t shift[8];
   int32_t bits[8];
-  // Shared memory layout.
-  int32_t rs[8];          // row stride (bytes) of plane p's packed rows
-  int32_t plane_base[8];  // offset of plane p's rows inside the data area
-  int32_t meta_off, data_off;
+  // Shared memory layout (bytes from the start of dynamic shared memory).
+  int32_t rowoff_off, meta_off, data_off;
   uint32_t* err;
 };
 
@@ -86,61 +89,123 @@ __device__ __forceinline__ int mode_bits(const TileArgs& a, int p) {
   else return a.bits[p];
 }
 
+// Tile geometry; compile-time constants when DT != 0.
+template <int DT>
+struct Geo {
+  int D, TT, O, A;
+  __device__ __forceinline__ explicit Geo(const TileArgs& a)
+      : D(DT ? DT : a.D),
+        TT(DT ? tile_tokens_for(DT) : a.TT),
+        O((DT ? DT : a.D) >> 3),
+        A((DT ? tile_tokens_for(DT) : a.TT) >> 3) {}
+  // (x + y) mod O for x, y >= 0; O is a power of two when DT != 0.
+  __device__ __forceinline__ int rot(int x, int y) const {
+    if constexpr (DT != 0) return (x + y) & (O - 1);
+    else return (x + y) % O;
+  }
+};
+
+template <int MODE, int DT>
+__device__ __forceinline__ int plane_stride(const TileArgs& a, const Geo<DT>& g, int p, bool restore) {
+  return run_stride(g.TT, mode_bits<MODE>(a, p), restore);
+}
+
+template <int MODE, int DT>
+__device__ __forceinline__ int plane_base(const TileArgs& a, const Geo<DT>& g, int p, bool restore) {
+  int base = 0;
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    if (q >= p) break;
+    base += g.D * plane_stride<MODE, DT>(a, g, q, restore);
+  }
+  return base;
+}
+
 struct TileCoord {
   int kv, h, n;
   int64_t t0;
 };
 
-__device__ __forceinline__ TileCoord tile_coord(const TileArgs& args) {
+__device__ __forceinline__ TileCoord tile_coord(const TileArgs& args, int TT) {
   int tile = blockIdx.x;
   const int tt = tile % args.tiles_per_head;
   tile /= args.tiles_per_head;
   TileCoord tc;
   tc.h = tile % args.H;
   tc.kv = tile / args.H;
-  tc.t0 = static_cast<int64_t>(tt) * args.TT;
-  tc.n = static_cast<int>(min64(static_cast<int64_t>(args.TT), args.T - tc.t0));
+  tc.t0 = static_cast<int64_t>(tt) * TT;
+  tc.n = static_cast<int>(min64(static_cast<int64_t>(TT), args.T - tc.t0));
   return tc;
 }
 
-// spec_of_c[c] = index of the spec covering (h, c), -1 when none does.
-__device__ __forceinline__ void scan_specs(const TileArgs& args, int h, int16_t* spec_of_c) {
-  for (int c = threadIdx.x; c < args.D; c += kThreads) spec_of_c[c] = -1;
+// spec_of_c[c] = index of the spec covering (h, c), -1 when none does. rowoff[t] = element
+// offset of token t0 + t of (kv, h) in the rows tensor, -1 when its block id is invalid
+// (counted in args.err). One block-table lookup per token row and tile.
+__device__ __forceinline__ void tile_setup(const TileArgs& args, const TileCoord& tc, int D, int16_t* spec_of_c,
+                                           int64_t* rowoff) {
+  for (int c = threadIdx.x; c < D; c += kThreads) spec_of_c[c] = -1;
+  const int32_t bs = static_cast<int32_t>(args.block_size);
+  for (int t = threadIdx.x; t < tc.n; t += kThreads) {
+    const int32_t tg = static_cast<int32_t>(tc.t0) + t;
+    const int32_t bi = tg / bs;
+    const int64_t blk = args.block_ids ? args.block_ids[bi] : bi;
+    if (blk < 0 || blk >= args.num_blocks) {
+      rowoff[t] = -1;
+      if (args.err) atomicAdd(args.err, 1u);
+    } else {
+      rowoff[t] = tc.kv * args.kv_stride + blk * args.block_stride +
+                  static_cast<int64_t>(tg - bi * bs) * args.token_stride +
+                  static_cast<int64_t>(tc.h) * args.head_stride;
+    }
+  }
   __syncthreads();
   for (int s = threadIdx.x; s < args.S; s += kThreads) {
     const int64_t* sp = args.specs + 6 * static_cast<int64_t>(s);
-    if (sp[0] <= h && h < sp[1]) {
+    if (sp[0] <= tc.h && tc.h < sp[1]) {
       for (int64_t c = sp[2]; c < sp[3]; ++c) spec_of_c[c] = static_cast<int16_t>(s);
     }
   }
   __syncthreads();
 }
 
-__device__ __forceinline__ int64_t row_element(const TileArgs& args, int kv, int h, int64_t tg,
-                                               int64_t& blk) {
-  const int64_t bi = tg / args.block_size;
-  blk = args.block_ids ? args.block_ids[bi] : bi;
-  return kv * args.kv_stride + blk * args.block_stride + (tg - bi * args.block_size) * args.token_stride +
-         static_cast<int64_t>(h) * args.head_stride;
+// Copy one 8-channel chunk of a token row between shared memory and global memory.
+template <int ELEM>
+__device__ __forceinline__ void store_chunk(uint8_t* gdst, const uint8_t* ssrc) {
+  if constexpr (ELEM == 2) st_global_cs16(gdst, *reinterpret_cast<const uint4*>(ssrc));
+  else st_global_cs8(gdst, *reinterpret_cast<const uint2*>(ssrc));
+}
+
+template <int ELEM>
+__device__ __forceinline__ void load_chunk_async(uint8_t* sdst, const uint8_t* gsrc) {
+  if constexpr (ELEM == 2) cp_async16(sdst, gsrc);
+  else cp_async8(sdst, gsrc);
+}
+
+template <int ELEM>
+__device__ __forceinline__ void zero_chunk(uint8_t* sdst) {
+  if constexpr (ELEM == 2) *reinterpret_cast<uint4*>(sdst) = make_uint4(0u, 0u, 0u, 0u);
+  else *reinterpret_cast<uint2*>(sdst) = make_uint2(0u, 0u);
 }
 
 // ---------------------------------------------------------------------------------------
 // Restore: packed chunks -> rows
 // ---------------------------------------------------------------------------------------
-template <int ELEM, int MODE>
+template <int ELEM, int MODE, int DT>
 __global__ void __launch_bounds__(kThreads) restore_tiles(const TileArgs args) {
   extern __shared__ __align__(128) uint8_t smem[];
   int16_t* spec_of_c = reinterpret_cast<int16_t*>(smem);
+  int64_t* rowoff = reinterpret_cast<int64_t*>(smem + args.rowoff_off);
   RowMeta* meta = reinterpret_cast<RowMeta*>(smem + args.meta_off);
   uint8_t* data = smem + args.data_off;
   const int tid = threadIdx.x;
-  const int D = args.D;
+  const Geo<DT> g(args);
+  const int D = g.D;
+  const int O = g.O;
   const int P = mode_planes<MODE>(args);
-  const TileCoord tc = tile_coord(args);
+  const TileCoord tc = tile_coord(args, g.TT);
 
-  scan_specs(args, tc.h, spec_of_c);
+  tile_setup(args, tc, D, spec_of_c, rowoff);
 
-  // Per-run metadata.
   for (int r = tid; r < P * D; r += kThreads) {
     const int p = r / D;
     const int c = r - p * D;
@@ -167,27 +232,30 @@ __global__ void __launch_bounds__(kThreads) restore_tiles(const TileArgs args) {
   __syncthreads();
 
   // Phase A: stage the covering 16-byte words of every run.
+#pragma unroll 1
   for (int p = 0; p < P; ++p) {
-    const int W = args.rs[p] >> 4;
+    const int rs = plane_stride<MODE, DT>(args, g, p, true);
+    const int W = rs >> 4;
     const int cnt = D * W;
-    uint8_t* pbase = data + args.plane_base[p];
+    uint8_t* pbase = data + plane_base<MODE, DT>(args, g, p, true);
+    const RowMeta* pm = meta + p * D;
     for (int i = tid; i < cnt; i += kThreads) {
       const int c = i / W;
       const int w = i - c * W;
-      const RowMeta m = meta[p * D + c];
-      uint8_t* dst = pbase + c * args.rs[p] + w * 16;
-      if (m.a < 0) {
+      const int64_t ma = pm[c].a;
+      uint8_t* dst = pbase + c * rs + w * 16;
+      if (ma < 0) {
         *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
         continue;
       }
-      if (w >= m.b) continue;
-      const int64_t g = m.a + 16 * static_cast<int64_t>(w);
-      if (g + 16 <= args.packed_bytes) {
-        cp_async16(dst, args.packed + g);
+      if (w >= pm[c].b) continue;
+      const int64_t gofs = ma + 16 * static_cast<int64_t>(w);
+      if (gofs + 16 <= args.packed_bytes) {
+        cp_async16(dst, args.packed + gofs);
       } else {
         uint32_t v[4] = {0u, 0u, 0u, 0u};
         for (int j = 0; j < 16; ++j) {
-          if (g + j < args.packed_bytes) v[j >> 2] |= static_cast<uint32_t>(args.packed[g + j]) << (8 * (j & 3));
+          if (gofs + j < args.packed_bytes) v[j >> 2] |= static_cast<uint32_t>(args.packed[gofs + j]) << (8 * (j & 3));
         }
         *reinterpret_cast<uint4*>(dst) = make_uint4(v[0], v[1], v[2], v[3]);
       }
@@ -197,8 +265,7 @@ __global__ void __launch_bounds__(kThreads) restore_tiles(const TileArgs args) {
   __syncthreads();
 
   // Phase B: 8 tokens x 8 channels per thread.
-  const int A = args.TT >> 3;
-  const int O = D >> 3;
+  const int A = g.A;
   const bool have = tid < A * O;
   const int a = tid % A;
   const int o = tid / A;
@@ -215,16 +282,24 @@ __global__ void __launch_bounds__(kThreads) restore_tiles(const TileArgs args) {
     for (int p = 0; p < (MODE == kModeGeneric ? 8 : 3); ++p) {
       if (p >= P) break;
       uint32_t lo[8], hi[8];
-      const uint8_t* pbase = data + args.plane_base[p];
+      const int rs = plane_stride<MODE, DT>(args, g, p, true);
+      const uint8_t* pbase = data + plane_base<MODE, DT>(args, g, p, true);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const int c = 8 * o + j;
         const int mc = meta[p * D + c].c;
         const int bits = MODE == kModeGeneric ? (mc >> 16) : mode_bits<MODE>(args, p);
-        const int bitpos = (mc & 0xFFFF) + 8 * a * bits;
-        uint32_t v0, v1;
-        window64(pbase + c * args.rs[p], bitpos, v0, v1);
-        spread8_rt(v0, v1, bits, lo[j], hi[j]);
+        const int bit0 = mc & 0xFFFF;
+        const uint8_t* row = pbase + c * rs;
+        if (bits == 8 && (bit0 & 63) == 0) {
+          const uint2 v = *reinterpret_cast<const uint2*>(row + (bit0 >> 3) + 8 * a);
+          lo[j] = v.x;
+          hi[j] = v.y;
+        } else {
+          uint32_t v0, v1;
+          window64(row, bit0 + 8 * a * bits, v0, v1);
+          spread8_rt(v0, v1, bits, lo[j], hi[j]);
+        }
       }
       transpose8x8(lo, hi);  // row i = token i: channels 0..3 in lo, 4..7 in hi
       if constexpr (ELEM == 1) {
@@ -264,7 +339,7 @@ __global__ void __launch_bounds__(kThreads) restore_tiles(const TileArgs args) {
   __syncthreads();  // every packed run has been consumed; reuse the area for rows
   const int row_bytes = D * ELEM;
   if (have) {
-    const int phys = (o + a) % O;
+    const int phys = g.rot(o, a);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       uint8_t* dst = data + (8 * a + i) * row_bytes + phys * (8 * ELEM);
@@ -279,22 +354,21 @@ __global__ void __launch_bounds__(kThreads) restore_tiles(const TileArgs args) {
 
   // Phase C: rows to the destination.
   uint8_t* rows = static_cast<uint8_t*>(args.rows);
-  for (int i = tid; i < tc.n * O; i += kThreads) {
-    const int t = i / O;
-    const int oc = i - t * O;
-    int64_t blk;
-    const int64_t e = row_element(args, tc.kv, tc.h, tc.t0 + t, blk);
-    if (blk < 0 || blk >= args.num_blocks) {
-      if (oc == 0 && args.err) atomicAdd(args.err, 1u);
-      continue;
+  if (kThreads % O == 0) {  // fixed chunk per thread, rows strided
+    const int oc = tid % O;
+    const int step = kThreads / O;
+    for (int t = tid / O; t < tc.n; t += step) {
+      const int64_t off = rowoff[t];
+      if (off < 0) continue;
+      store_chunk<ELEM>(rows + (off + 8 * oc) * ELEM, data + t * row_bytes + g.rot(oc, t >> 3) * (8 * ELEM));
     }
-    const int phys = (oc + (t >> 3)) % O;
-    const uint8_t* src = data + t * row_bytes + phys * (8 * ELEM);
-    uint8_t* dst = rows + (e + 8 * oc) * ELEM;
-    if constexpr (ELEM == 2) {
-      st_global_cs16(dst, *reinterpret_cast<const uint4*>(src));
-    } else {
-      st_global_cs8(dst, *reinterpret_cast<const uint2*>(src));
+  } else {
+    for (int i = tid; i < tc.n * O; i += kThreads) {
+      const int t = i / O;
+      const int oc = i - t * O;
+      const int64_t off = rowoff[t];
+      if (off < 0) continue;
+      store_chunk<ELEM>(rows + (off + 8 * oc) * ELEM, data + t * row_bytes + g.rot(oc, t >> 3) * (8 * ELEM));
     }
   }
 }
@@ -302,18 +376,49 @@ __global__ void __launch_bounds__(kThreads) restore_tiles(const TileArgs args) {
 // ---------------------------------------------------------------------------------------
 // Pack: rows -> packed chunks
 // ---------------------------------------------------------------------------------------
-template <int ELEM, int MODE>
+
+// One destination 32-bit word W of a run whose stream bits are [B, E) and whose first
+// nsrc bits come from `src` (a 16-byte aligned shared row; bits past nsrc are zero pad):
+// plain store when the run owns the whole word, otherwise a masked atomic clear + set of
+// the run's own bits (the neighbouring run owns the rest of the word).
+__device__ __forceinline__ void put_word(uint32_t* dst32, int64_t W, int64_t B, int64_t E, int64_t nsrc,
+                                         const uint32_t* src) {
+  const int64_t rel = W * 32 - B;
+  const int64_t nsw = (nsrc + 31) >> 5;
+  const int64_t q = rel >> 5;
+  const int r = static_cast<int>(rel & 31);
+  const uint32_t lo = (q >= 0 && q < nsw) ? src[q] : 0u;
+  const uint32_t hi = (q + 1 >= 0 && q + 1 < nsw) ? src[q + 1] : 0u;
+  uint32_t v = __funnelshift_r(lo, hi, r);
+  const int vlo = static_cast<int>(min64(max64(-rel, 0), 32));
+  const int vhi = static_cast<int>(min64(max64(nsrc - rel, 0), 32));
+  v &= bit_range_mask(vlo, vhi);
+  const int olo = static_cast<int>(min64(max64(B - W * 32, 0), 32));
+  const int ohi = static_cast<int>(min64(max64(E - W * 32, 0), 32));
+  const uint32_t own = bit_range_mask(olo, ohi);
+  if (own == 0xFFFFFFFFu) {
+    dst32[W] = v;
+  } else if (own != 0u) {
+    atomicAnd(dst32 + W, ~own);
+    atomicOr(dst32 + W, v & own);
+  }
+}
+
+template <int ELEM, int MODE, int DT>
 __global__ void __launch_bounds__(kThreads) pack_tiles(const TileArgs args) {
   extern __shared__ __align__(128) uint8_t smem[];
   int16_t* spec_of_c = reinterpret_cast<int16_t*>(smem);
+  int64_t* rowoff = reinterpret_cast<int64_t*>(smem + args.rowoff_off);
   RowMeta* meta = reinterpret_cast<RowMeta*>(smem + args.meta_off);
   uint8_t* data = smem + args.data_off;
   const int tid = threadIdx.x;
-  const int D = args.D;
+  const Geo<DT> g(args);
+  const int D = g.D;
+  const int O = g.O;
   const int P = mode_planes<MODE>(args);
-  const TileCoord tc = tile_coord(args);
+  const TileCoord tc = tile_coord(args, g.TT);
 
-  scan_specs(args, tc.h, spec_of_c);
+  tile_setup(args, tc, D, spec_of_c, rowoff);
 
   for (int r = tid; r < P * D; r += kThreads) {
     const int p = r / D;
@@ -341,36 +446,38 @@ __global__ void __launch_bounds__(kThreads) pack_tiles(const TileArgs args) {
   }
 
   // Phase A: stage the tile's rows; 8-channel chunks rotated by token octet.
-  const int O = D >> 3;
   const int row_bytes = D * ELEM;
   const uint8_t* rows = static_cast<const uint8_t*>(args.rows);
-  for (int i = tid; i < tc.n * O; i += kThreads) {
-    const int t = i / O;
-    const int oc = i - t * O;
-    int64_t blk;
-    const int64_t e = row_element(args, tc.kv, tc.h, tc.t0 + t, blk);
-    uint8_t* dst = data + t * row_bytes + ((oc + (t >> 3)) % O) * (8 * ELEM);
-    if (blk < 0 || blk >= args.num_blocks) {
-      if (oc == 0 && args.err) atomicAdd(args.err, 1u);
-      if constexpr (ELEM == 2) *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
-      else *reinterpret_cast<uint2*>(dst) = make_uint2(0u, 0u);
-      continue;
+  if (kThreads % O == 0) {
+    const int oc = tid % O;
+    const int step = kThreads / O;
+    for (int t = tid / O; t < tc.n; t += step) {
+      const int64_t off = rowoff[t];
+      uint8_t* dst = data + t * row_bytes + g.rot(oc, t >> 3) * (8 * ELEM);
+      if (off < 0) zero_chunk<ELEM>(dst);
+      else load_chunk_async<ELEM>(dst, rows + (off + 8 * oc) * ELEM);
     }
-    const uint8_t* src = rows + (e + 8 * oc) * ELEM;
-    if constexpr (ELEM == 2) cp_async16(dst, src);
-    else cp_async8(dst, src);
+  } else {
+    for (int i = tid; i < tc.n * O; i += kThreads) {
+      const int t = i / O;
+      const int oc = i - t * O;
+      const int64_t off = rowoff[t];
+      uint8_t* dst = data + t * row_bytes + g.rot(oc, t >> 3) * (8 * ELEM);
+      if (off < 0) zero_chunk<ELEM>(dst);
+      else load_chunk_async<ELEM>(dst, rows + (off + 8 * oc) * ELEM);
+    }
   }
   cp_async_wait_all();
   __syncthreads();
 
-  const int A = args.TT >> 3;
+  const int A = g.A;
   const bool have = tid < A * O;
   const int a = tid % A;
   const int o = tid / A;
   constexpr int WPT = ELEM == 2 ? 4 : 2;
   uint32_t x[8][WPT];
   if (have) {
-    const int phys = (o + a) % O;
+    const int phys = g.rot(o, a);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const uint8_t* src = data + (8 * a + i) * row_bytes + phys * (8 * ELEM);
@@ -397,8 +504,7 @@ __global__ void __launch_bounds__(kThreads) pack_tiles(const TileArgs args) {
       if constexpr (ELEM == 1) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          // one plane per symbol tensor; masking happens per chunk below
-          lo[i] = x[i][0];
+          lo[i] = x[i][0];  // masked per chunk below
           hi[i] = x[i][1];
         }
       } else if constexpr (MODE == kModeByte2) {
@@ -419,12 +525,13 @@ __global__ void __launch_bounds__(kThreads) pack_tiles(const TileArgs args) {
         }
       }
       transpose8x8(lo, hi);  // row j = channel j: tokens 0..3 in lo, 4..7 in hi
-      uint8_t* pbase = data + args.plane_base[p];
+      const int rs = plane_stride<MODE, DT>(args, g, p, false);
+      uint8_t* pbase = data + plane_base<MODE, DT>(args, g, p, false);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const int c = 8 * o + j;
         const int bits = MODE == kModeGeneric ? meta[p * D + c].c : mode_bits<MODE>(args, p);
-        uint8_t* row = pbase + c * args.rs[p];
+        uint8_t* row = pbase + c * rs;
         if (bits == 8) {
           *reinterpret_cast<uint2*>(row + 8 * a) = make_uint2(lo[j], hi[j]);
         } else {
@@ -438,43 +545,44 @@ __global__ void __launch_bounds__(kThreads) pack_tiles(const TileArgs args) {
   }
   __syncthreads();
 
-  // Phase C: runs to the chunk stream. Fully owned words: plain stores; words shared
-  // with a neighbouring run: masked atomic clear + set of this run's bits only.
+  // Phase C: runs to the chunk stream in 16-byte destination vectors.
   uint32_t* dst32 = reinterpret_cast<uint32_t*>(args.packed);
+#pragma unroll 1
   for (int p = 0; p < P; ++p) {
-    const int maxbits = MODE == kModeGeneric ? 8 : mode_bits<MODE>(args, p);
-    const int Wmax = ((args.TT * maxbits + 7 + 31) >> 5) + 1;
-    const int cnt = D * Wmax;
-    const uint8_t* pbase = data + args.plane_base[p];
+    const int maxbits = MODE == kModeGeneric ? args.bits[p] : mode_bits<MODE>(args, p);
+    const int Vmax = ((g.TT * maxbits + 7 + 127) >> 7) + 1;
+    const int cnt = D * Vmax;
+    const int rs = plane_stride<MODE, DT>(args, g, p, false);
+    const uint8_t* pbase = data + plane_base<MODE, DT>(args, g, p, false);
+    const RowMeta* pm = meta + p * D;
     for (int i = tid; i < cnt; i += kThreads) {
-      const int c = i / Wmax;
-      const int w = i - c * Wmax;
-      const RowMeta m = meta[p * D + c];
-      if (m.a < 0) continue;
-      const int64_t B = m.a;
-      const int64_t E = B + m.b;
-      const int64_t W = (B >> 5) + w;
-      if (W > ((E - 1) >> 5)) continue;
-      const int64_t rel = W * 32 - B;
-      const int64_t nsrc = static_cast<int64_t>(tc.n) * m.c;
-      const int64_t nsw = (nsrc + 31) >> 5;
-      const uint32_t* src = reinterpret_cast<const uint32_t*>(pbase + c * args.rs[p]);
-      const int64_t q = rel >> 5;
-      const int r = static_cast<int>(rel & 31);
-      const uint32_t lo = (q >= 0 && q < nsw) ? src[q] : 0u;
-      const uint32_t hi = (q + 1 >= 0 && q + 1 < nsw) ? src[q + 1] : 0u;
-      uint32_t v = __funnelshift_r(lo, hi, r);
-      const int vlo = static_cast<int>(min64(max64(-rel, 0), 32));
-      const int vhi = static_cast<int>(min64(max64(nsrc - rel, 0), 32));
-      v &= bit_range_mask(vlo, vhi);
-      const int olo = static_cast<int>(min64(max64(B - W * 32, 0), 32));
-      const int ohi = static_cast<int>(min64(max64(E - W * 32, 0), 32));
-      const uint32_t own = bit_range_mask(olo, ohi);
-      if (own == 0xFFFFFFFFu) {
-        dst32[W] = v;
-      } else if (own != 0u) {
-        atomicAnd(dst32 + W, ~own);
-        atomicOr(dst32 + W, v & own);
+      const int c = i / Vmax;
+      const int v = i - c * Vmax;
+      const int64_t B = pm[c].a;
+      if (B < 0) continue;
+      const int64_t E = B + pm[c].b;
+      const int64_t V = (B >> 7) + v;
+      if (V > ((E - 1) >> 7)) continue;
+      const int64_t nsrc = static_cast<int64_t>(tc.n) * pm[c].c;
+      const uint32_t* src = reinterpret_cast<const uint32_t*>(pbase + c * rs);
+      const int64_t rel = V * 128 - B;  // source bit of the vector's first bit
+      if ((B & 31) == 0 && rel >= 0 && rel + 128 <= nsrc && V * 128 + 128 <= E) {
+        // fully owned, word aligned vector made of source bits only
+        const int q = static_cast<int>(rel >> 5);
+        uint4 w;
+        if ((q & 3) == 0) {
+          w = *reinterpret_cast<const uint4*>(src + q);
+        } else {
+          w = make_uint4(src[q], src[q + 1], src[q + 2], src[q + 3]);
+        }
+        st_global_cs16(dst32 + 4 * V, w);
+      } else {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int64_t W = 4 * V + k;
+          if (W * 32 + 32 <= B || W * 32 >= E) continue;
+          put_word(dst32, W, B, E, nsrc, src);
+        }
       }
     }
   }
