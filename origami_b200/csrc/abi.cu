@@ -8,8 +8,13 @@
 #include <vector>
 
 #include "../../include/origami_b200.h"
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
 #include "linear_kernels.cuh"
 #include "tile_kernels.cuh"
+#include "tma_kernels.cuh"
 
 namespace {
 
@@ -194,13 +199,57 @@ int32_t validate_cache(const origami_paged_kv* kv, PagedGeom& g) {
   return ORIGAMI_OK;
 }
 
+// Dynamic shared memory is raised per (kernel, device) to the largest size ever launched
+// (the attribute is a maximum, so it never has to go down); resident CTAs for a
+// persistent launch (SMs x blocks per SM) are cached per (kernel, device, size).
+int32_t persistent_slots(const void* fn, int smem, int& resident) {
+  struct Attr {
+    const void* fn;
+    int dev, smem_max;
+  };
+  struct Occ {
+    const void* fn;
+    int dev, smem, slots;
+  };
+  static std::mutex mu;
+  static std::vector<Attr> attrs;
+  static std::vector<Occ> occ;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  std::lock_guard<std::mutex> lock(mu);
+  Attr* a = nullptr;
+  for (Attr& x : attrs)
+    if (x.fn == fn && x.dev == dev) a = &x;
+  if (a == nullptr || a->smem_max < smem) {
+    if ((e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess)
+      return cuda_fail(e, "cudaFuncSetAttribute");
+    if (a == nullptr) attrs.push_back({fn, dev, smem});
+    else a->smem_max = smem;
+  }
+  for (const Occ& x : occ)
+    if (x.fn == fn && x.dev == dev && x.smem == smem) {
+      resident = x.slots;
+      return ORIGAMI_OK;
+    }
+  int sms = 0, per_sm = 0;
+  if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+    return cuda_fail(e, "cudaDeviceGetAttribute");
+  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kThreads, smem)) != cudaSuccess)
+    return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+  resident = sms * std::max(per_sm, 1);
+  occ.push_back({fn, dev, smem, resident});
+  return ORIGAMI_OK;
+}
+
 template <int ELEM, int MODE, int DT>
 int32_t launch_tiles(bool restore, TileArgs& a, size_t smem, cudaStream_t st) {
   const void* fn = restore ? reinterpret_cast<const void*>(&origami::restore_tiles<ELEM, MODE, DT>)
                            : reinterpret_cast<const void*>(&origami::pack_tiles<ELEM, MODE, DT>);
   if (smem > 48 * 1024) {
-    const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+    int resident = 0;  // sets the shared-memory attribute once per (kernel, device, size)
+    const int32_t rc = persistent_slots(fn, static_cast<int>(smem), resident);
+    if (rc) return rc;
   }
   const int64_t tiles = static_cast<int64_t>(a.num_kv) * a.H * a.tiles_per_head;
   if (tiles <= 0) return ORIGAMI_OK;
@@ -334,6 +383,103 @@ int32_t canonical_common(bool restore, const uint8_t* d_packed, int64_t packed_b
   return after_launch("canon_pack_linear launch");
 }
 
+// ---------------------------------------------------------------------------------------
+// TMA path for the aligned plane format (see tma_kernels.cuh).
+// ---------------------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// True when every (kv, plane) component is a dense [H*D runs][T*bits/8] byte array in
+// canonical order with 16-byte aligned rows, and the tile boxes are 16-byte multiples.
+bool tma_eligible(int mode, const std::vector<Spec>& specs, const int64_t* off, const origami_planes* pl,
+                  int64_t T, int64_t H, int64_t D, const uint8_t* packed) {
+  if (mode == origami::kModeGeneric) return false;
+  if (D != 64 && D != 128 && D != 256) return false;
+  if (!aligned(packed, 16)) return false;
+  const int TT = tile_tokens(D);
+  const int64_t S = static_cast<int64_t>(specs.size());
+  const int P = pl->num_planes;
+  for (int q = 0; q < 2 * P; ++q) {
+    const int b = pl->bits[q % P];
+    if ((T * b) % 128 != 0 || (TT * b) % 128 != 0 || TT * b / 8 > 256) return false;
+    const int64_t run = T * b / 8;
+    const int64_t base = off[q * S];
+    if (base % 16 != 0) return false;
+    for (int64_t s = 0; s < S; ++s) {
+      if (off[q * S + s] != base + (specs[s].h0 * D + specs[s].c0) * run) return false;
+    }
+  }
+  return H * D <= 0x7FFFFFFF && T * 8 <= 0x7FFFFFFF;
+}
+
+template <int MODE, int D>
+int32_t launch_tma(bool restore, const origami_paged_kv* cache, const PagedGeom& g, const int64_t* d_block_ids,
+                   int64_t T, const origami_planes* pl, const int64_t* off, int64_t S, uint8_t* packed,
+                   uint32_t* d_err, cudaStream_t st) {
+  using G = origami::TmaGeo<MODE, D>;
+  auto encode = tensor_map_encoder();
+  if (encode == nullptr) return fail(ORIGAMI_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  origami::TmaArgs a{};
+  const int P = G::P;
+  for (int q = 0; q < 2 * P; ++q) {
+    const int b = G::bits(q % P);
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(T * b / 8), static_cast<cuuint64_t>(cache->num_heads * D)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(T * b / 8)};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(G::TT * b / 8), static_cast<cuuint32_t>(D)};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = encode(&a.maps[q], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, packed + off[q * S], dims, strides, box,
+                              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(ORIGAMI_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  }
+  a.rows = cache->d_data;
+  a.kv_stride = g.kv_stride;
+  a.block_stride = g.block_stride;
+  a.token_stride = g.token_stride;
+  a.head_stride = g.head_stride;
+  a.block_size = cache->block_size;
+  a.num_blocks = cache->num_blocks;
+  a.block_ids = d_block_ids;
+  a.T = T;
+  a.H = static_cast<int32_t>(cache->num_heads);
+  a.tiles_per_head = static_cast<int32_t>((T + G::TT - 1) / G::TT);
+  const int64_t tiles = 2 * cache->num_heads * a.tiles_per_head;
+  if (tiles > 0x7FFFFFFF) return fail(ORIGAMI_ERR_UNSUPPORTED, "too many tiles");
+  a.num_tiles = static_cast<int32_t>(tiles);
+  a.err = d_err;
+  const void* fn = restore ? reinterpret_cast<const void*>(&origami::restore_tma<MODE, D>)
+                           : reinterpret_cast<const void*>(&origami::pack_tma<MODE, D>);
+  const int smem = restore ? G::smem_bytes : origami::PackGeo<MODE, D>::smem_bytes;
+  int resident = 0;
+  int32_t rc = persistent_slots(fn, smem, resident);
+  if (rc) return rc;
+  const int grid = static_cast<int>(std::min<int64_t>(tiles, resident));
+  if (restore) origami::restore_tma<MODE, D><<<grid, kThreads, smem, st>>>(a);
+  else origami::pack_tma<MODE, D><<<grid, kThreads, smem, st>>>(a);
+  return after_launch(restore ? "restore_tma launch" : "pack_tma launch");
+}
+
+template <int MODE>
+int32_t launch_tma_by_dim(bool restore, int64_t D, const origami_paged_kv* cache, const PagedGeom& g,
+                          const int64_t* ids, int64_t T, const origami_planes* pl, const int64_t* off, int64_t S,
+                          uint8_t* packed, uint32_t* err, cudaStream_t st) {
+  switch (D) {
+    case 64: return launch_tma<MODE, 64>(restore, cache, g, ids, T, pl, off, S, packed, err, st);
+    case 128: return launch_tma<MODE, 128>(restore, cache, g, ids, T, pl, off, S, packed, err, st);
+    default: return launch_tma<MODE, 256>(restore, cache, g, ids, T, pl, off, S, packed, err, st);
+  }
+}
+
 int32_t layer_common(bool restore, const origami_paged_kv* cache, const int64_t* d_block_ids,
                      int64_t num_block_ids, int64_t T, const origami_planes* planes,
                      const origami_chunk_table* table, uint8_t* d_packed, int64_t packed_bytes,
@@ -380,6 +526,21 @@ int32_t layer_common(bool restore, const origami_paged_kv* cache, const int64_t*
                 (long long)off[nchunks]);
   if (d_packed == nullptr || !aligned(d_packed, 16)) return fail(ORIGAMI_ERR_INVALID, "packed buffer must be 16-byte aligned");
 
+  const int mode = classify_planes(*planes);
+  if (tma_eligible(mode, specs, off, planes, T, H, D, d_packed)) {
+    switch (mode) {
+      case origami::kModeByte2:
+        return launch_tma_by_dim<origami::kModeByte2>(restore, D, cache, g, d_block_ids, T, planes, off, S, d_packed,
+                                                      d_err, st);
+      case origami::kModeBf16Bits:
+        return launch_tma_by_dim<origami::kModeBf16Bits>(restore, D, cache, g, d_block_ids, T, planes, off, S,
+                                                         d_packed, d_err, st);
+      default:
+        return launch_tma_by_dim<origami::kModeFp16Bits>(restore, D, cache, g, d_block_ids, T, planes, off, S,
+                                                         d_packed, d_err, st);
+    }
+  }
+
   TileArgs a{};
   a.rows = cache->d_data;
   a.kv_stride = g.kv_stride;
@@ -409,7 +570,7 @@ int32_t layer_common(bool restore, const origami_paged_kv* cache, const int64_t*
   a.err = d_err;
   const size_t smem = layout_tile_smem(a, 2, restore, planes->bits);
   if (smem > 227 * 1024) return fail(ORIGAMI_ERR_UNSUPPORTED, "tile needs %zu bytes of shared memory", smem);
-  return dispatch_tiles(restore, 2, classify_planes(*planes), a, smem, st);
+  return dispatch_tiles(restore, 2, mode, a, smem, st);
 }
 
 int32_t slab_geometry(const origami_paged_kv* cache, int64_t num_block_ids, int64_t bytes, int64_t& slab,

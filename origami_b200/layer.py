@@ -161,6 +161,20 @@ def scatter_blocks(value: torch.Tensor, kv_layer: torch.Tensor, block_ids, *,
     _lib.check(rc, "origami_scatter_blocks")
 
 
+def fused_kernel_name(fmt: LayerFormat, restore: bool = True) -> str:
+    """Name of the kernel the fused op launches for this format: the persistent TMA
+    kernels for aligned preset formats, the generic tile kernels otherwise (the rule of
+    tma_eligible in csrc/abi.cu; the packed buffer is assumed 16-byte aligned)."""
+    presets = {(8, 0): (8, 8), (7, 15, 0): (8, 1, 7), (10, 8, 0): (6, 2, 8)}
+    D, T = fmt.head_dim, fmt.num_tokens
+    tt = 8 * (2048 // D)
+    aligned = (presets.get(tuple(fmt.planes.shifts)) == tuple(fmt.planes.bits) and D in (64, 128, 256)
+               and all((T * b) % 128 == 0 and (tt * b) % 128 == 0 for b in fmt.planes.bits))
+    if aligned:
+        return "restore_tma" if restore else "pack_tma"
+    return "restore_tiles" if restore else "pack_tiles"
+
+
 def raw_chunk_bounds(total_bytes: int, chunk_bytes: int = 1 << 20) -> np.ndarray:
     """Byte bounds of the reference's raw-bytes chunks: the planner over a
     [1, 1, total_bytes] symbol tensor yields contiguous slices (chunking.py:95-121)."""

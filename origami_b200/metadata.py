@@ -44,3 +44,42 @@ class LayerPayload:
     quantizer: str
     quant_metadata: dict[str, Any]
     chunks: list[ChunkRecord] = field(default_factory=list)
+
+
+@dataclass
+class OrigamiPayload:
+    cache_key: str
+    request_id: str
+    quantizer: str
+    quantizer_config_hash: str
+    token_start: int
+    token_count: int
+    layer_payloads: dict[str, LayerPayload] = field(default_factory=dict)
+    metadata: dict[str, Any] = field(default_factory=dict)
+
+
+@dataclass(frozen=True)
+class OrigamiRestoreRequest:
+    request_id: str
+    cache_key: str
+    block_ids_per_group: tuple[tuple[int, ...], ...]
+    num_tokens: int
+    lossless_path: str = "cpu"
+    metric_request_id: str | None = None
+
+
+@dataclass(frozen=True)
+class OrigamiSaveRequest:
+    request_id: str
+    cache_key: str
+    block_ids_per_group: tuple[tuple[int, ...], ...]
+    num_tokens: int
+    token_start: int = 0
+
+
+@dataclass
+class OrigamiConnectorMetadata:
+    """What the scheduler side hands the worker each step (metadata.py:74-92)."""
+
+    reqs_to_restore: dict[str, OrigamiRestoreRequest] = field(default_factory=dict)
+    reqs_to_save: dict[str, OrigamiSaveRequest] = field(default_factory=dict)

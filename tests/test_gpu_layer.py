@@ -19,6 +19,9 @@ GEOMS = [
     (4096, 16, 2, 128, 1 << 16),
     (8191, 16, 1, 128, 100_000),
     (70, 16, 3, 8, 1 << 20),
+    (1040, 16, 2, 128, 1 << 20),  # aligned runs, partial last tile (TMA path for byte planes)
+    (2048, 32, 4, 64, 1 << 20),
+    (512, 16, 2, 256, 1 << 20),
 ]
 PLANES = [BYTE_PLANES, BF16_BIT_PLANES, FP16_BIT_PLANES, ODD_PLANES]
 
