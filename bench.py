@@ -47,6 +47,8 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="bound on the CPU baseline sample")
+    ap.add_argument("--no-pipeline", action="store_true", help="skip the C4 exposed-restore measurement")
+    ap.add_argument("--pipeline-layers", type=int, default=8, help="C4 layers sampled by the pipeline measurement")
     return ap.parse_args()
 
 
@@ -321,6 +323,11 @@ def run_origami(args, rank, world, local):
 
     k_restore, k_pack = fused_kernel_name(wl.fmt, True), fused_kernel_name(wl.fmt, False)
 
+    pipeline_info = None
+    if not args.no_pipeline:
+        pipeline_info = run_pipeline_c4(args, device, world)
+        ok = ok and pipeline_info.pop("ok")
+
     e2e = None
     if not args.no_e2e:
         e2e = run_e2e(args, wl, device, world)
@@ -375,6 +382,8 @@ def run_origami(args, rank, world, local):
     }
     if e2e is not None:
         result["e2e"] = e2e
+    if pipeline_info is not None:
+        result["pipeline"] = pipeline_info
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(args, wl)
     if rank == 0:
@@ -429,6 +438,119 @@ def run_e2e(args, wl, device, world):
             "ms_per_step": round(ms / args.steps, 3), "pcie_h2d_gbs": round(h2d * args.steps / (ms / 1e3) / GB, 2),
             "gpu_launches": pipe.launches - launches0, "pipeline": "pinned host -> copy stream -> 3-slot ring -> "
             "restore stream, per-layer events", "ok": ok}
+
+
+def run_pipeline_c4(args, device, world):
+    """Exposed restore time per layer for one rank of C4 (Llama-3-70B KV at TP=8: 1 KV head,
+    4 x 131072 tokens, fp16, block 32): per-layer pinned H2D + restore through
+    RestorePipeline overlapped with a bf16 8192^3 prefill GEMM per layer on the model's
+    stream, which waits on each layer's event (the wait_for_layer_load contract)."""
+    import torch
+
+    from origami_b200 import BYTE_PLANES, LayerFormat, workloads
+    from origami_b200.layer import pack_layer
+    from origami_b200.pipeline import RestorePipeline
+
+    cfg = workloads.C4
+    L = max(2, args.pipeline_layers)
+    heads, T, bs, R = 1, cfg.tokens[0], cfg.block_size, len(cfg.tokens)
+    nb = T // bs
+    fmt = LayerFormat(T, heads, cfg.head_dim, BYTE_PLANES)
+    pool = workloads.permuted_block_table(nb * R, nb * R, workloads.SEED + 4)
+    ids = [pool[r * nb:(r + 1) * nb].to(device) for r in range(R)]
+    caches, hosts, origs = [], [], []
+    for layer in range(L):
+        cache = torch.empty((2, nb * R, bs, heads, cfg.head_dim), dtype=cfg.dtype, device=device)
+        row = []
+        for r in range(R):
+            kv = workloads.kv_values(T, heads, cfg.head_dim, cfg.dtype, seed=workloads.SEED + 77 * layer + r,
+                                     v_std=cfg.v_std, device=device)
+            workloads.scatter_into_cache(cache, kv, ids[r])
+            h = torch.empty((fmt.packed_bytes,), dtype=torch.uint8, pin_memory=True)
+            h.copy_(pack_layer(cache, ids[r], fmt))
+            row.append(h)
+        origs.append(cache.clone())
+        caches.append(cache)
+        hosts.append(row)
+    torch.cuda.synchronize(device)
+    a = torch.randn((8192, 8192), dtype=torch.bfloat16, device=device)
+    b = torch.randn((8192, 8192), dtype=torch.bfloat16, device=device)
+    c = torch.empty((8192, 8192), dtype=torch.bfloat16, device=device)
+    model = torch.cuda.Stream(device)
+    pipe = RestorePipeline(device, fmt.packed_bytes, slots=3)
+    err = torch.zeros(1, dtype=torch.int32, device=device)
+
+    def timed(fn):
+        torch.cuda.synchronize(device)
+        barrier(world)
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(model)
+        fn()
+        t1.record(model)
+        torch.cuda.synchronize(device)
+        return max_over_ranks(t0.elapsed_time(t1), world, device)
+
+    def compute_only():
+        with torch.cuda.stream(model):
+            for _ in range(L):
+                torch.matmul(a, b, out=c)
+
+    def restore_only():
+        ev = None
+        pipe.copy_stream.wait_stream(model)
+        for layer in range(L):
+            for r in range(R):
+                ev = pipe.enqueue(hosts[layer][r], fmt, caches[layer], ids[r], error_count=err)
+        model.wait_event(ev)
+
+    def pipelined():
+        pipe.copy_stream.wait_stream(model)
+        evs = [[pipe.enqueue(hosts[layer][r], fmt, caches[layer], ids[r], error_count=err) for r in range(R)]
+               for layer in range(L)]
+        with torch.cuda.stream(model):
+            for layer in range(L):
+                for ev in evs[layer]:
+                    model.wait_event(ev)  # wait_for_layer_load(layer)
+                torch.matmul(a, b, out=c)
+
+    def unpipelined():
+        from origami_b200.layer import restore_layer
+
+        slot = pipe.slots[0].buf
+        with torch.cuda.stream(model):
+            for layer in range(L):
+                for r in range(R):
+                    slot[: fmt.packed_bytes].copy_(hosts[layer][r], non_blocking=True)
+                    restore_layer(slot[: fmt.packed_bytes], fmt, caches[layer], ids[r], stream=model, error_count=err)
+
+    for fn in (compute_only, restore_only, pipelined, unpipelined):  # warm-up
+        fn()
+    for cc in caches:
+        cc.zero_()
+    t_compute = timed(compute_only)
+    t_restore = timed(restore_only)
+    t_unpipe = timed(unpipelined)
+    for cc in caches:
+        cc.zero_()
+    t_pipe = timed(pipelined)
+    ok = all(torch.equal(x.view(torch.int16), y.view(torch.int16)) for x, y in zip(caches, origs)) and int(err.item()) == 0
+    exposed = (t_pipe - t_compute) / L
+    unpipe_per_layer = t_unpipe / L
+    h2d_bytes = L * R * fmt.packed_bytes
+    return {
+        "workload": f"C4 one rank at TP=8: {L} of 80 layers, 1 KV head, {R} x {T} tokens, fp16, block {bs}, "
+                    "byte planes; per layer a bf16 8192x8192x8192 GEMM on the model stream",
+        "exposed_restore_ms_per_layer": round(exposed, 4),
+        "unpipelined_restore_ms_per_layer": round(unpipe_per_layer, 4),
+        "exposed_frac_of_unpipelined": round(exposed / unpipe_per_layer, 4),
+        "compute_only_ms_per_layer": round(t_compute / L, 4),
+        "restore_only_ms_per_layer": round(t_restore / L, 4),
+        "pipelined_ms_per_layer": round(t_pipe / L, 4),
+        "pcie_h2d_gbs": round(h2d_bytes / (t_restore / 1e3) / GB, 2),
+        "overlap_frac_of_ideal": round((t_compute + t_restore - t_pipe) / min(t_compute, t_restore), 4),
+        "bytes_per_layer": R * fmt.packed_bytes,
+        "ok": ok,
+    }
 
 
 def cpu_baseline(args, wl):
