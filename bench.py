@@ -30,6 +30,8 @@ import threading
 import time
 from pathlib import Path
 
+import numpy as np
+
 REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO))
 
@@ -43,7 +45,9 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("origami", "reference"), default="origami")
     ap.add_argument("--planes", default="byte", help="byte | bit | bf16_bits | fp16_bits")
-    ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--layers", type=int, default=0, help="layers (default: 32 for C2, 4 for C3, 8 for C5)")
+    ap.add_argument("--config", choices=("C2", "C3", "C5"), default="C2", help="workload (C2 is the headline)")
+    ap.add_argument("--chunk-bytes", type=int, default=1 << 20, help="codec chunk size (min = target = max)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="bound on the CPU baseline sample")
@@ -176,43 +180,101 @@ def profiled_traffic(kernel: str, workload: str):
 # workload
 # ----------------------------------------------------------------------------------------
 class Workload:
-    """C2 at weak scaling: `world` requests of 32768 tokens, heads sharded by rank."""
+    """One rank's share of a benchmark configuration (heads sharded by rank).
 
-    def __init__(self, rank: int, world: int, layers: int, planes_name: str, device):
+    C2  restore, weak scaling: `world` requests of 32768 tokens, 8/N heads per rank.
+    C3  restore, strong scaling: 16 ragged requests (T ~ U[4096, 65536]) with interleaved
+        block tables in a pool sized for 120 GB (57,220 blocks), 8/N heads per rank.
+    C5  save, strong scaling: 64 requests x 8192 tokens of Qwen2-7B KV, 4/N heads per rank.
+    """
+
+    def __init__(self, config: str, rank: int, world: int, layers: int, planes_name: str, device,
+                 chunk_bytes: int = 1 << 20):
         import torch
 
         from origami_b200 import LayerFormat, plane_spec, workloads
         from origami_b200.layer import pack_layer
 
-        cfg = workloads.C2
+        self.config = config
+        if config == "C2":
+            cfg = workloads.C2
+            tokens = [cfg.tokens[0]] * world
+            self.scaling = "weak"
+        elif config == "C3":
+            cfg = workloads.c3_config()
+            tokens = list(cfg.tokens)
+            self.scaling = "strong"
+        elif config == "C5":
+            cfg = workloads.C5
+            tokens = list(cfg.tokens)
+            self.scaling = "strong"
+        else:
+            raise SystemExit(f"unknown config {config!r}")
         if cfg.heads % world:
             raise SystemExit(f"{cfg.heads} KV heads do not shard over {world} ranks")
         self.cfg = cfg
         self.layers = layers
         self.heads = cfg.heads // world
         self.head0 = rank * self.heads
-        self.requests = world
-        self.T = cfg.tokens[0]
+        self.tokens = tokens
+        self.requests = len(tokens)
         self.bs = cfg.block_size
-        nb = self.T // self.bs
-        self.NB = nb * self.requests
+        nbs = [(t + self.bs - 1) // self.bs for t in tokens]
         self.planes = plane_spec(planes_name, cfg.dtype)
-        self.fmt = LayerFormat(self.T, self.heads, cfg.head_dim, self.planes)
-        pool = workloads.permuted_block_table(self.NB, self.NB, workloads.SEED)
-        self.block_ids = [pool[r * nb:(r + 1) * nb].to(device) for r in range(self.requests)]
-        self.caches, self.packed, self.orig = [], [], []
+        fmts: dict[int, LayerFormat] = {}
+        for t in tokens:
+            if t not in fmts:
+                fmts[t] = LayerFormat(t, self.heads, cfg.head_dim, self.planes, chunk_bytes, chunk_bytes, chunk_bytes)
+        self.fmts = [fmts[t] for t in tokens]
+        if config == "C2":
+            self.NB = sum(nbs)
+            pool = workloads.permuted_block_table(self.NB, self.NB, workloads.SEED)
+            starts = np.concatenate([[0], np.cumsum(nbs)])
+            tables = [pool[int(a):int(b)] for a, b in zip(starts[:-1], starts[1:])]
+        else:
+            self.NB = workloads.c3_pool_blocks(cfg) if config == "C3" else sum(nbs)
+            tables = workloads.interleaved_block_tables(tokens, self.bs, self.NB, workloads.SEED + 5)
+        self.block_ids = [t.to(device) for t in tables]
+        # Requests with the same token count share a format; each format group keeps its
+        # (layer, request) jobs in one packed arena at a uniform 16-byte-multiple stride,
+        # so a step is one batched call per group.
+        from origami_b200.layer import alloc_jobs_packed, job_stride
+
+        self.groups = []  # (fmt, [(layer, r)], arena)
+        by_t: dict[int, list[int]] = {}
+        for r, t in enumerate(tokens):
+            by_t.setdefault(t, []).append(r)
+        self.packed = [[None] * self.requests for _ in range(layers)]
+        for t, reqs in by_t.items():
+            fmt = fmts[t]
+            jobs = [(layer, r) for layer in range(layers) for r in reqs]
+            arena = alloc_jobs_packed(fmt, len(jobs), device)
+            stride = job_stride(fmt)
+            for j, (layer, r) in enumerate(jobs):
+                self.packed[layer][r] = arena[j * stride:j * stride + fmt.packed_bytes]
+            self.groups.append((fmt, jobs, arena))
+        self.caches, self.orig = [], []
         for layer in range(layers):
-            cache = torch.empty((2, self.NB, self.bs, self.heads, cfg.head_dim), dtype=cfg.dtype, device=device)
-            per_req = []
+            cache = torch.zeros((2, self.NB, self.bs, self.heads, cfg.head_dim), dtype=cfg.dtype, device=device)
             for r in range(self.requests):
-                kv = workloads.kv_values(self.T, cfg.heads, cfg.head_dim, cfg.dtype, seed=workloads.SEED + 1000 * layer + r,
-                                         v_std=cfg.v_std, device=device)[:, :, self.head0:self.head0 + self.heads]
+                kv = workloads.kv_values(tokens[r], cfg.heads, cfg.head_dim, cfg.dtype,
+                                         seed=workloads.SEED + 1000 * layer + r, v_std=cfg.v_std,
+                                         device=device)[:, :, self.head0:self.head0 + self.heads]
                 workloads.scatter_into_cache(cache, kv.contiguous(), self.block_ids[r])
-                per_req.append(pack_layer(cache, self.block_ids[r], self.fmt))
+                pack_layer(cache, self.block_ids[r], self.fmts[r], out=self.packed[layer][r])
             self.orig.append(cache.clone())
             self.caches.append(cache)
-            self.packed.append(per_req)
         torch.cuda.synchronize()
+
+    def kernel_launches(self) -> int:
+        """Kernels one batched pass launches (128 jobs per persistent TMA launch; the
+        generic tile path launches once per job)."""
+        from origami_b200.layer import fused_kernel_name
+
+        n = 0
+        for fmt, jobs, _ in self.groups:
+            n += (len(jobs) + 127) // 128 if fused_kernel_name(fmt).endswith("tma") else len(jobs)
+        return n
 
     @property
     def units_per_step(self) -> int:
@@ -220,11 +282,15 @@ class Workload:
 
     @property
     def kv_bytes_per_step(self) -> int:
-        return self.units_per_step * self.fmt.kv_bytes
+        return self.layers * sum(f.kv_bytes for f in self.fmts)
 
     @property
     def packed_bytes_per_step(self) -> int:
-        return self.units_per_step * self.fmt.packed_bytes
+        return self.layers * sum(f.packed_bytes for f in self.fmts)
+
+    @property
+    def max_packed(self) -> int:
+        return max(f.packed_bytes for f in self.fmts)
 
     def verify(self) -> bool:
         import torch
@@ -235,37 +301,38 @@ class Workload:
 def run_origami(args, rank, world, local):
     import torch
 
-    from origami_b200.layer import pack_layer, restore_layer
-    from origami_b200.pipeline import RestorePipeline
+    from origami_b200.layer import fused_kernel_name, pack_layers, restore_layers
 
     device = torch.device("cuda", local)
-    wl = Workload(rank, world, args.layers, args.planes, device)
+    layers = args.layers if args.layers else {"C2": 32, "C3": 4, "C5": 8}[args.config]
+    wl = Workload(args.config, rank, world, layers, args.planes, device, args.chunk_bytes)
     stream = torch.cuda.current_stream(device)
     err = torch.zeros(1, dtype=torch.int32, device=device)
 
-    # the originals are kept; zero the caches so the timed restores rebuild them
-    for c in wl.caches:
-        c.zero_()
+    def zero_caches():
+        # the originals are kept; zero the caches so the timed restores rebuild them
+        for c in wl.caches:
+            c.zero_()
 
     def restore_step(events=None):
-        for layer in range(wl.layers):
-            for r in range(wl.requests):
-                if events is not None:
-                    events.append((torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)))
-                    events[-1][0].record(stream)
-                restore_layer(wl.packed[layer][r], wl.fmt, wl.caches[layer], wl.block_ids[r], error_count=err)
-                if events is not None:
-                    events[-1][1].record(stream)
+        for fmt, jobs, arena in wl.groups:
+            if events is not None:
+                events.append((torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)))
+                events[-1][0].record(stream)
+            restore_layers(arena, fmt, [wl.caches[layer] for layer, _ in jobs], [wl.block_ids[r] for _, r in jobs],
+                           error_count=err)
+            if events is not None:
+                events[-1][1].record(stream)
 
     def pack_step(events=None):
-        for layer in range(wl.layers):
-            for r in range(wl.requests):
-                if events is not None:
-                    events.append((torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)))
-                    events[-1][0].record(stream)
-                pack_layer(wl.caches[layer], wl.block_ids[r], wl.fmt, out=wl.packed[layer][r], error_count=err)
-                if events is not None:
-                    events[-1][1].record(stream)
+        for fmt, jobs, arena in wl.groups:
+            if events is not None:
+                events.append((torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)))
+                events[-1][0].record(stream)
+            pack_layers([wl.caches[layer] for layer, _ in jobs], [wl.block_ids[r] for _, r in jobs], fmt, arena,
+                        error_count=err)
+            if events is not None:
+                events[-1][1].record(stream)
 
     host_us_per_call = []
 
@@ -283,7 +350,7 @@ def run_origami(args, rank, world, local):
         step_fn(launch_events)
         host_us = (time.perf_counter() - t_host) * 1e6 / max(1, len(launch_events))
         torch.cuda.synchronize(device)
-        launch_ms = statistics.mean(a.elapsed_time(b) for a, b in launch_events)
+        launch_ms_sum = sum(a.elapsed_time(b) for a, b in launch_events)
         host_us_per_call.append(host_us)
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
@@ -301,82 +368,100 @@ def run_origami(args, rank, world, local):
         barrier(world)
         ms = t0.elapsed_time(t1)
         del graph
-        return max_over_ranks(ms, world, device), launch_ms, len(launch_events) * args.steps
+        return max_over_ranks(ms, world, device), launch_ms_sum, wl.kernel_launches()
 
+    primary_pack = args.config == "C5"
     clocks = ClockSampler(local)
     clocks.start()
-    restore_ms, restore_launch_ms, restore_launches = timed(restore_step)
-    clock_info = clocks.stop()
-    ok = wl.verify() and int(err.item()) == 0
-    pack_ms, pack_launch_ms, pack_launches = timed(pack_step)
+    if primary_pack:
+        pack_ms, pack_sum, launches = timed(pack_step)
+        clock_info = clocks.stop()
+        ok = wl.verify() and int(err.item()) == 0
+        zero_caches()
+        restore_ms, restore_sum, _ = timed(restore_step)
+    else:
+        zero_caches()
+        restore_ms, restore_sum, launches = timed(restore_step)
+        clock_info = clocks.stop()
+        ok = wl.verify() and int(err.item()) == 0
+        pack_ms, pack_sum, _ = timed(pack_step)
     ok = ok and wl.verify() and int(err.item()) == 0
 
     steps = args.steps
-    total_kv = wl.kv_bytes_per_step * world * steps
-    value = total_kv / (restore_ms / 1e3) / GB
     peak, peak_kind = measured_hbm_peak()
-    alg_restore = wl.fmt.packed_bytes + wl.fmt.kv_bytes
-    achieved = alg_restore / (restore_launch_ms / 1e3) / GB
-    achieved_pack = alg_restore / (pack_launch_ms / 1e3) / GB
-    workload_name = f"C2_restore_T{wl.T}_H{wl.heads}_D{wl.cfg.head_dim}_{wl.planes.name}"
-    from origami_b200.layer import fused_kernel_name
-
-    k_restore, k_pack = fused_kernel_name(wl.fmt, True), fused_kernel_name(wl.fmt, False)
+    alg_step = wl.packed_bytes_per_step + wl.kv_bytes_per_step  # per rank, one pass
+    restore_gbs = wl.kv_bytes_per_step * world * steps / (restore_ms / 1e3) / GB
+    pack_gbs = wl.kv_bytes_per_step * world * steps / (pack_ms / 1e3) / GB
+    achieved_restore = alg_step / (restore_sum / 1e3) / GB
+    achieved_pack = alg_step / (pack_sum / 1e3) / GB
+    kinds = {fused_kernel_name(f, True) for f in wl.fmts}
+    k_restore = "/".join(sorted(kinds))
+    k_pack = "/".join(sorted({fused_kernel_name(f, False) for f in wl.fmts}))
+    workload_name = (f"C2_restore_T{wl.tokens[0]}_H{wl.heads}_D{wl.cfg.head_dim}_{wl.planes.name}"
+                     if args.config == "C2" and args.chunk_bytes == 1 << 20 else None)
+    roof_restore = {"kernel": k_restore, "bound": "hbm", "achieved": round(achieved_restore, 1), "peak": peak,
+                    "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved_restore / peak, 4),
+                    "traffic": profiled_traffic(k_restore, workload_name) if workload_name else None,
+                    "algorithmic_bytes_per_launch": alg_step // launches,
+                    "launch_ms": round(restore_sum / launches, 5),
+                    "host_us_per_call": round(host_us_per_call[0 if not primary_pack else 1], 1)}
+    roof_pack = {"kernel": k_pack, "bound": "hbm", "achieved": round(achieved_pack, 1), "peak": peak,
+                 "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved_pack / peak, 4),
+                 "traffic": profiled_traffic(k_pack, workload_name) if workload_name else None,
+                 "algorithmic_bytes_per_launch": alg_step // launches,
+                 "launch_ms": round(pack_sum / launches, 5)}
 
     pipeline_info = None
-    if not args.no_pipeline:
+    if not args.no_pipeline and args.config == "C2":
         pipeline_info = run_pipeline_c4(args, device, world)
         ok = ok and pipeline_info.pop("ok")
 
     e2e = None
     if not args.no_e2e:
-        e2e = run_e2e(args, wl, device, world)
+        e2e = run_e2e_save(args, wl, device, world) if primary_pack else run_e2e(args, wl, device, world)
         ok = ok and e2e.pop("ok")
 
+    cfg_desc = {
+        "C2": "C2: Llama-3-8B-shaped KV restore, 32768-token request per GPU, seeded block-table permutation",
+        "C3": "C3: batched ragged restore, 16 requests T~U[4096,65536], interleaved block tables, 120 GB pool",
+        "C5": "C5: save-path stress, Qwen2-7B KV, 64 requests x 8192 tokens, gather+plane split+bitpack",
+    }[args.config]
+    if primary_pack:
+        metric = "KV pack GB/s (gather + plane split + bitpack), whole job"
+        value, ms_step, roof = pack_gbs, pack_ms / steps, roof_pack
+        secondary = {"restore": {"value": round(restore_gbs, 1), "unit": "GB/s",
+                                 "ms_per_step": round(restore_ms / steps, 4), "roofline": roof_restore}}
+    else:
+        metric = "KV restore GB/s (unpack + plane merge + paged scatter), whole job"
+        value, ms_step, roof = restore_gbs, restore_ms / steps, roof_restore
+        secondary = {"pack": {"metric": "KV pack GB/s (gather + plane split + bitpack), whole job",
+                              "value": round(pack_gbs, 1), "unit": "GB/s", "ms_per_step": round(pack_ms / steps, 4),
+                              "roofline": roof_pack}}
     result = {
-        "metric": "KV restore GB/s (unpack + plane merge + paged scatter), whole job",
+        "metric": metric,
         "value": round(value, 1),
         "unit": "GB/s",
         "n_gpus": world,
         "steps": steps,
         "warmup": args.warmup,
-        "ms_per_step": round(restore_ms / steps, 4),
+        "ms_per_step": round(ms_step, 4),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": wl.scaling,
         "vs_baseline": None,
-        "dtype": "u16 (bf16 bit patterns)",
+        "dtype": "u16 (bf16/fp16 bit patterns)",
         "data": "synthetic (seeded N(0,1) x log-uniform channel scales, K outliers x20, V N(0,0.5))",
         "config": {
-            "workload": "C2: Llama-3-8B-shaped KV restore, 32768-token request, seeded block-table permutation",
-            "layers": wl.layers, "tokens_per_request": wl.T, "requests": wl.requests, "kv_heads": wl.cfg.heads,
-            "heads_per_rank": wl.heads, "head_dim": wl.cfg.head_dim, "block_size": wl.bs, "cache_dtype": "bf16",
-            "planes": wl.planes.name, "chunk_bytes": 1 << 20, "parallelism": f"kv-head shard x{world}, no collective",
+            "workload": cfg_desc,
+            "layers": wl.layers, "requests": wl.requests, "tokens_total": int(sum(wl.tokens)),
+            "kv_heads": wl.cfg.heads, "heads_per_rank": wl.heads, "head_dim": wl.cfg.head_dim,
+            "block_size": wl.bs, "cache_dtype": str(wl.cfg.dtype).replace("torch.", ""), "planes": wl.planes.name,
+            "chunk_bytes": args.chunk_bytes, "parallelism": f"kv-head shard x{world}, no collective",
             "l2": "inputs larger than L2 (%.1f GiB packed + %.1f GiB cache per rank per step)" % (
                 wl.packed_bytes_per_step / 2**30, wl.kv_bytes_per_step / 2**30),
         },
-        "roofline": {
-            "kernel": k_restore,
-            "bound": "hbm",
-            "achieved": round(achieved, 1),
-            "peak": peak,
-            "peak_kind": peak_kind,
-            "unit": "GB/s",
-            "frac": round(achieved / peak, 4),
-            "traffic": profiled_traffic(k_restore, workload_name),
-            "algorithmic_bytes_per_launch": alg_restore,
-            "launch_ms": round(restore_launch_ms, 5),
-            "host_us_per_call": round(host_us_per_call[0], 1),
-        },
-        "pack": {
-            "metric": "KV pack GB/s (gather + plane split + bitpack), whole job",
-            "value": round(wl.kv_bytes_per_step * world * steps / (pack_ms / 1e3) / GB, 1),
-            "unit": "GB/s",
-            "ms_per_step": round(pack_ms / steps, 4),
-            "roofline": {"kernel": k_pack, "bound": "hbm", "achieved": round(achieved_pack, 1), "peak": peak,
-                         "unit": "GB/s", "frac": round(achieved_pack / peak, 4),
-                         "traffic": profiled_traffic(k_pack, workload_name)},
-        },
-        "gpu_launches": restore_launches,
+        "roofline": roof,
+        **secondary,
+        "gpu_launches": launches * steps,
         "clocks": clock_info,
         "verified": bool(ok),
     }
@@ -397,7 +482,7 @@ def run_e2e(args, wl, device, world):
 
     from origami_b200.pipeline import RestorePipeline
 
-    host = [[torch.empty((wl.fmt.packed_bytes,), dtype=torch.uint8, pin_memory=True) for _ in range(wl.requests)]
+    host = [[torch.empty((wl.fmts[r].packed_bytes,), dtype=torch.uint8, pin_memory=True) for r in range(wl.requests)]
             for _ in range(wl.layers)]
     for layer in range(wl.layers):
         for r in range(wl.requests):
@@ -405,7 +490,7 @@ def run_e2e(args, wl, device, world):
     torch.cuda.synchronize(device)
     for c in wl.caches:
         c.zero_()
-    pipe = RestorePipeline(device, wl.fmt.packed_bytes, slots=3)
+    pipe = RestorePipeline(device, wl.max_packed, slots=3)
     err = torch.zeros(1, dtype=torch.int32, device=device)
     err_host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
 
@@ -413,7 +498,7 @@ def run_e2e(args, wl, device, world):
         ev = None
         for layer in range(wl.layers):
             for r in range(wl.requests):
-                ev = pipe.enqueue(host[layer][r], wl.fmt, wl.caches[layer], wl.block_ids[r], error_count=err)
+                ev = pipe.enqueue(host[layer][r], wl.fmts[r], wl.caches[layer], wl.block_ids[r], error_count=err)
         pipe.restore_stream.wait_event(ev)
         with torch.cuda.stream(pipe.restore_stream):
             err_host.copy_(err, non_blocking=True)
@@ -438,6 +523,54 @@ def run_e2e(args, wl, device, world):
             "ms_per_step": round(ms / args.steps, 3), "pcie_h2d_gbs": round(h2d * args.steps / (ms / 1e3) / GB, 2),
             "gpu_launches": pipe.launches - launches0, "pipeline": "pinned host -> copy stream -> 3-slot ring -> "
             "restore stream, per-layer events", "ok": ok}
+
+
+def run_e2e_save(args, wl, device, world):
+    """Save into pinned host chunks through SavePipeline (pack on a save stream, D2H on a
+    copy stream); the block tables go H2D every step; D2H inside the timed region."""
+    import torch
+
+    from origami_b200.pipeline import SavePipeline
+
+    host = [[torch.empty((wl.fmts[r].packed_bytes,), dtype=torch.uint8, pin_memory=True) for r in range(wl.requests)]
+            for _ in range(wl.layers)]
+    ids_host = [t.cpu().pin_memory() for t in wl.block_ids]
+    ids_dev = [torch.empty_like(t) for t in wl.block_ids]
+    pipe = SavePipeline(device, wl.max_packed, slots=3)
+    err = torch.zeros(1, dtype=torch.int32, device=device)
+
+    def step():
+        done = None
+        with torch.cuda.stream(pipe.save_stream):
+            for h, d in zip(ids_host, ids_dev):
+                d.copy_(h, non_blocking=True)
+        for layer in range(wl.layers):
+            for r in range(wl.requests):
+                done = pipe.enqueue(wl.caches[layer], ids_dev[r], wl.fmts[r], host[layer][r], error_count=err)
+        pipe.copy_stream.wait_event(done)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(device)
+    barrier(world)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(pipe.save_stream)
+    launches0 = pipe.launches
+    for _ in range(args.steps):
+        step()
+    t1.record(pipe.copy_stream)
+    torch.cuda.synchronize(device)
+    barrier(world)
+    ms = max_over_ranks(t0.elapsed_time(t1), world, device)
+    ok = all(torch.equal(host[layer][r][: wl.fmts[r].packed_bytes], wl.packed[layer][r].cpu())
+             for layer in range(wl.layers) for r in range(wl.requests)) and int(err.item()) == 0
+    value = wl.kv_bytes_per_step * world * args.steps / (ms / 1e3) / GB
+    d2h = wl.packed_bytes_per_step
+    return {"value": round(value, 1), "unit": "GB/s", "h2d_bytes_per_step": sum(t.numel() * 8 for t in ids_host),
+            "d2h_bytes_per_step": d2h, "ms_per_step": round(ms / args.steps, 3),
+            "pcie_d2h_gbs": round(d2h * args.steps / (ms / 1e3) / GB, 2),
+            "gpu_launches": pipe.launches - launches0,
+            "pipeline": "save stream pack -> 3-slot ring -> copy stream D2H into pinned host", "ok": ok}
 
 
 def run_pipeline_c4(args, device, world):
@@ -554,8 +687,8 @@ def run_pipeline_c4(args, device, world):
 
 
 def cpu_baseline(args, wl):
-    """The CPU oracle restore of a bounded sample of C2 layers on the host cores."""
-    import numpy as np
+    """The CPU oracle on the host cores over a bounded sample of the config's layers
+    (request 0): restore for C2/C3, pack for C5."""
     import torch
 
     sys.path.insert(0, str(REPO / "oracle"))
@@ -563,67 +696,86 @@ def cpu_baseline(args, wl):
 
     threads = os.cpu_count() or 1
     oracle.set_threads(threads)
-    packed = [wl.packed[layer][0].cpu().numpy() for layer in range(min(wl.layers, 8))]
+    fmt, T = wl.fmts[0], wl.tokens[0]
     ids = wl.block_ids[0].cpu().numpy()
-    cache = np.zeros((2, wl.NB, wl.bs, wl.heads, wl.cfg.head_dim), dtype=np.uint16)
+    pack_dir = args.config == "C5"
+    layers = min(wl.layers, 8)
+    if pack_dir:
+        caches = [o.cpu().view(torch.int16).numpy().view(np.uint16) for o in wl.orig[:layers]]
+    else:
+        packed = [wl.packed[layer][0].cpu().numpy() for layer in range(layers)]
+        cache = np.zeros((2, wl.NB, wl.bs, wl.heads, wl.cfg.head_dim), dtype=np.uint16)
     done = 0
     t0 = time.perf_counter()
-    while done < len(packed):
-        oracle.restore_layer(packed[done], wl.planes.shifts, wl.planes.bits, wl.fmt.specs, cache, 0, ids, wl.T)
+    while done < layers:
+        if pack_dir:
+            oracle.pack_layer(caches[done], 0, ids, T, wl.planes.shifts, wl.planes.bits, fmt.specs)
+        else:
+            oracle.restore_layer(packed[done], wl.planes.shifts, wl.planes.bits, fmt.specs, cache, 0, ids, T)
         done += 1
         if time.perf_counter() - t0 > args.cpu_seconds:
             break
     dt = time.perf_counter() - t0
-    return {"value": round(done * wl.fmt.kv_bytes / dt / GB, 3), "unit": "GB/s", "cores": oracle.max_threads(),
-            "kind": "port", "sample": f"{done} C2 layers x 1 request ({done * wl.fmt.kv_bytes / 2**20:.0f} MiB KV), "
-            f"oracle restore_layer, {dt:.1f} s"}
+    what = "pack_layer" if pack_dir else "restore_layer"
+    return {"value": round(done * fmt.kv_bytes / dt / GB, 3), "unit": "GB/s", "cores": oracle.max_threads(),
+            "kind": "port", "sample": f"{done} {args.config} layers x 1 request ({done * fmt.kv_bytes / 2**20:.0f} MiB "
+            f"KV), oracle {what}, {dt:.1f} s"}
 
 
 def run_reference(args, rank, world):
-    """CPU implementation of the path on the host cores (rank 0 only)."""
+    """CPU implementation of the path on the host cores (rank 0 only): the oracle port of
+    the reference layout on one request of the config per step (restore; pack for C5)."""
     if rank != 0:
         return 0
-    import numpy as np
+    import torch
 
     sys.path.insert(0, str(REPO / "oracle"))
     import oracle
     from origami_b200 import LayerFormat, plane_spec, workloads
 
-    cfg = workloads.C2
+    cfg = {"C2": workloads.C2, "C3": workloads.c3_config(), "C5": workloads.C5}[args.config]
     heads = cfg.heads // world
     T, bs = cfg.tokens[0], cfg.block_size
-    nb = T // bs
+    nb = (T + bs - 1) // bs
     planes = plane_spec(args.planes, cfg.dtype)
-    fmt = LayerFormat(T, heads, cfg.head_dim, planes)
+    cb = args.chunk_bytes
+    fmt = LayerFormat(T, heads, cfg.head_dim, planes, cb, cb, cb)
     threads = os.cpu_count() or 1
     oracle.set_threads(threads)
     ids = workloads.permuted_block_table(nb, nb, workloads.SEED).numpy()
-    import torch
-
     kv = workloads.kv_values(T, cfg.heads, cfg.head_dim, cfg.dtype, seed=workloads.SEED, v_std=cfg.v_std)
     cache = torch.zeros((2, nb, bs, heads, cfg.head_dim), dtype=cfg.dtype)
     workloads.scatter_into_cache(cache, kv[:, :, :heads].contiguous(), torch.from_numpy(ids))
     c16 = cache.view(torch.int16).numpy().view(np.uint16).copy()
     packed, _ = oracle.pack_layer(c16, 0, ids, T, planes.shifts, planes.bits, fmt.specs)
     dst = np.zeros_like(c16)
-    # one step = one layer of one request (a bounded sample of the C2 step)
+    pack_dir = args.config == "C5"
+
+    def step():
+        if pack_dir:
+            oracle.pack_layer(c16, 0, ids, T, planes.shifts, planes.bits, fmt.specs)
+        else:
+            oracle.restore_layer(packed, planes.shifts, planes.bits, fmt.specs, dst, 0, ids, T)
+
     for _ in range(args.warmup):
-        oracle.restore_layer(packed, planes.shifts, planes.bits, fmt.specs, dst, 0, ids, T)
+        step()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        oracle.restore_layer(packed, planes.shifts, planes.bits, fmt.specs, dst, 0, ids, T)
+        step()
     dt = time.perf_counter() - t0
-    ok = bool(np.array_equal(dst, c16))
+    ok = True if pack_dir else bool(np.array_equal(dst, c16))
     value = fmt.kv_bytes * args.steps / dt / GB
-    sample = f"1 C2 layer x 1 request per step ({fmt.kv_bytes / 2**20:.0f} MiB KV), {heads} heads"
+    sample = f"1 {args.config} layer x 1 request per step ({fmt.kv_bytes / 2**20:.0f} MiB KV), {heads} heads"
+    metric = ("KV pack GB/s (gather + plane split + bitpack), whole job" if pack_dir else
+              "KV restore GB/s (unpack + plane merge + paged scatter), whole job")
     line = {
         "impl": "reference",
-        "metric": "KV restore GB/s (unpack + plane merge + paged scatter), whole job",
+        "metric": metric,
         "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(dt * 1e3 / args.steps, 2), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "u16 (bf16 bit patterns)", "data": "synthetic",
-        "config": {"workload": "C2: Llama-3-8B-shaped KV restore, 32768-token request (bounded CPU sample)",
-                   "planes": planes.name},
+        "ms_per_step": round(dt * 1e3 / args.steps, 2), "higher_is_better": True,
+        "scaling": "weak" if args.config == "C2" else "strong",
+        "vs_baseline": None, "dtype": "u16 (bf16/fp16 bit patterns)", "data": "synthetic",
+        "config": {"workload": f"{args.config} (bounded CPU sample)", "planes": planes.name, "chunk_bytes": cb},
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": oracle.max_threads(), "kind": "port",
                          "sample": sample},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},

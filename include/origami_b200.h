@@ -159,6 +159,33 @@ int32_t origami_restore_layer_to_paged(
     const int64_t* d_block_ids, int64_t num_block_ids, int64_t num_tokens,
     uint32_t* d_error_count, origami_stream_t stream);
 
+/* One job of a batched layer op: a layer (or a request) whose packed bytes start at
+ * d_packed + j * job_stride and whose rows live in d_kv_cache (the shared geometry). */
+typedef struct origami_layer_job {
+  void* d_kv_cache;
+  const int64_t* d_block_ids; /* int64, device */
+  int64_t num_block_ids;
+} origami_layer_job;
+
+/* Batched restore of num_jobs layers / requests that share one chunk table (same token
+ * count, heads, head_dim, planes and chunk sizes) and cache geometry (`cache`; its d_data
+ * is not used), in as few launches as possible. job_stride is a multiple of 16 bytes and
+ * at least h_offsets[last]; d_packed holds packed_bytes bytes. Same results as one
+ * origami_restore_layer_to_paged per job. No counterpart in the reference, which restores
+ * one layer of one request per call (worker.py:1087-1248): batching amortises the launch
+ * tail over a whole step. */
+int32_t origami_restore_layers_to_paged(
+    const uint8_t* d_packed, int64_t packed_bytes, int64_t job_stride, const origami_planes* planes,
+    const origami_chunk_table* table, const origami_paged_kv* cache, const origami_layer_job* jobs,
+    int32_t num_jobs, int64_t num_tokens, uint32_t* d_error_count, origami_stream_t stream);
+
+/* Batched save: the inverse of origami_restore_layers_to_paged (same job conventions);
+ * job j's chunks are written at d_packed + j * job_stride. */
+int32_t origami_pack_layers_from_paged(
+    const origami_paged_kv* cache, const origami_layer_job* jobs, int32_t num_jobs, int64_t num_tokens,
+    const origami_planes* planes, const origami_chunk_table* table, uint8_t* d_packed, int64_t packed_bytes,
+    int64_t job_stride, uint32_t* d_error_count, origami_stream_t stream);
+
 /* ---------------------------------------------------------------------------------
  * Raw-bytes path (the reference's lossless RawBytesTensorAdapter layout)
  * ------------------------------------------------------------------------------- */

@@ -50,6 +50,14 @@ class ChunkTable(ctypes.Structure):
     ]
 
 
+class LayerJob(ctypes.Structure):
+    _fields_ = [
+        ("d_kv_cache", _vp),
+        ("d_block_ids", _vp),
+        ("num_block_ids", ctypes.c_int64),
+    ]
+
+
 class OrigamiError(RuntimeError):
     """A liborigami_b200 entry point returned an error status."""
 
@@ -74,6 +82,12 @@ def _declare(L: ctypes.CDLL) -> None:
     L.origami_pack_layer_from_paged.restype = i32
     L.origami_restore_layer_to_paged.argtypes = [_vp, i64, P(Planes), P(ChunkTable), P(PagedKV), _vp, i64, i64, _vp, _vp]
     L.origami_restore_layer_to_paged.restype = i32
+    L.origami_restore_layers_to_paged.argtypes = [_vp, i64, i64, P(Planes), P(ChunkTable), P(PagedKV), P(LayerJob),
+                                                  i32, i64, _vp, _vp]
+    L.origami_restore_layers_to_paged.restype = i32
+    L.origami_pack_layers_from_paged.argtypes = [P(PagedKV), P(LayerJob), i32, i64, P(Planes), P(ChunkTable), _vp,
+                                                 i64, i64, _vp, _vp]
+    L.origami_pack_layers_from_paged.restype = i32
     L.origami_gather_blocks.argtypes = [P(PagedKV), _vp, i64, _vp, i64, _vp, _vp]
     L.origami_gather_blocks.restype = i32
     L.origami_scatter_blocks.argtypes = [_vp, i64, P(PagedKV), _vp, i64, _vp, _vp]
@@ -111,6 +125,8 @@ EXPORTS = (
     "origami_pack_canonical_storage_chunks",
     "origami_pack_layer_from_paged",
     "origami_restore_layer_to_paged",
+    "origami_restore_layers_to_paged",
+    "origami_pack_layers_from_paged",
     "origami_gather_blocks",
     "origami_scatter_blocks",
 )

@@ -422,70 +422,93 @@ bool tma_eligible(int mode, const std::vector<Spec>& specs, const int64_t* off, 
   return H * D <= 0x7FFFFFFF && T * 8 <= 0x7FFFFFFF;
 }
 
+struct Job {
+  void* rows;
+  const int64_t* ids;
+  int64_t num_ids;
+};
+
 template <int MODE, int D>
-int32_t launch_tma(bool restore, const origami_paged_kv* cache, const PagedGeom& g, const int64_t* d_block_ids,
-                   int64_t T, const origami_planes* pl, const int64_t* off, int64_t S, uint8_t* packed,
-                   uint32_t* d_err, cudaStream_t st) {
+int32_t launch_tma(bool restore, const origami_paged_kv* cache, const PagedGeom& g, const Job* jobs, int num_jobs,
+                   int64_t T, const int64_t* off, int64_t S, uint8_t* packed, int64_t job_stride, uint32_t* d_err,
+                   cudaStream_t st) {
   using G = origami::TmaGeo<MODE, D>;
   auto encode = tensor_map_encoder();
   if (encode == nullptr) return fail(ORIGAMI_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
-  origami::TmaArgs a{};
-  const int P = G::P;
-  for (int q = 0; q < 2 * P; ++q) {
-    const int b = G::bits(q % P);
-    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(T * b / 8), static_cast<cuuint64_t>(cache->num_heads * D)};
-    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(T * b / 8)};
-    const cuuint32_t box[2] = {static_cast<cuuint32_t>(G::TT * b / 8), static_cast<cuuint32_t>(D)};
-    const cuuint32_t estr[2] = {1, 1};
-    const CUresult r = encode(&a.maps[q], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, packed + off[q * S], dims, strides, box,
-                              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                              CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return fail(ORIGAMI_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
-  }
-  a.rows = cache->d_data;
-  a.kv_stride = g.kv_stride;
-  a.block_stride = g.block_stride;
-  a.token_stride = g.token_stride;
-  a.head_stride = g.head_stride;
-  a.block_size = cache->block_size;
-  a.num_blocks = cache->num_blocks;
-  a.block_ids = d_block_ids;
-  a.T = T;
-  a.H = static_cast<int32_t>(cache->num_heads);
-  a.tiles_per_head = static_cast<int32_t>((T + G::TT - 1) / G::TT);
-  const int64_t tiles = 2 * cache->num_heads * a.tiles_per_head;
-  if (tiles > 0x7FFFFFFF) return fail(ORIGAMI_ERR_UNSUPPORTED, "too many tiles");
-  a.num_tiles = static_cast<int32_t>(tiles);
-  a.err = d_err;
   const void* fn = restore ? reinterpret_cast<const void*>(&origami::restore_tma<MODE, D>)
                            : reinterpret_cast<const void*>(&origami::pack_tma<MODE, D>);
   const int smem = restore ? G::smem_bytes : origami::PackGeo<MODE, D>::smem_bytes;
   int resident = 0;
   int32_t rc = persistent_slots(fn, smem, resident);
   if (rc) return rc;
-  const int grid = static_cast<int>(std::min<int64_t>(tiles, resident));
-  if (restore) origami::restore_tma<MODE, D><<<grid, kThreads, smem, st>>>(a);
-  else origami::pack_tma<MODE, D><<<grid, kThreads, smem, st>>>(a);
-  return after_launch(restore ? "restore_tma launch" : "pack_tma launch");
+  const int P = G::P;
+  const int32_t tiles_per_head = static_cast<int32_t>((T + G::TT - 1) / G::TT);
+  const int64_t tiles_per_job = 2 * cache->num_heads * tiles_per_head;
+  for (int j0 = 0; j0 < num_jobs; j0 += origami::kMaxJobs) {
+    const int nj = std::min(num_jobs - j0, origami::kMaxJobs);
+    origami::TmaArgs a{};
+    uint8_t* base = packed + static_cast<int64_t>(j0) * job_stride;
+    for (int q = 0; q < 2 * P; ++q) {
+      const int b = G::bits(q % P);
+      const cuuint64_t dims[3] = {static_cast<cuuint64_t>(T * b / 8), static_cast<cuuint64_t>(cache->num_heads * D),
+                                  static_cast<cuuint64_t>(nj)};
+      const cuuint64_t strides[2] = {static_cast<cuuint64_t>(T * b / 8), static_cast<cuuint64_t>(job_stride)};
+      const cuuint32_t box[3] = {static_cast<cuuint32_t>(G::TT * b / 8), static_cast<cuuint32_t>(D), 1};
+      const cuuint32_t estr[3] = {1, 1, 1};
+      const CUresult r = encode(&a.maps[q], CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, base + off[q * S], dims, strides, box,
+                                estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      if (r != CUDA_SUCCESS) return fail(ORIGAMI_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+    }
+    for (int j = 0; j < nj; ++j) {
+      a.rows[j] = jobs[j0 + j].rows;
+      a.block_ids[j] = jobs[j0 + j].ids;
+    }
+    a.kv_stride = g.kv_stride;
+    a.block_stride = g.block_stride;
+    a.token_stride = g.token_stride;
+    a.head_stride = g.head_stride;
+    a.block_size = cache->block_size;
+    a.num_blocks = cache->num_blocks;
+    a.T = T;
+    a.H = static_cast<int32_t>(cache->num_heads);
+    a.tiles_per_head = tiles_per_head;
+    const int64_t tiles = tiles_per_job * nj;
+    if (tiles > 0x7FFFFFFF) return fail(ORIGAMI_ERR_UNSUPPORTED, "too many tiles");
+    a.tiles_per_job = static_cast<int32_t>(tiles_per_job);
+    a.num_tiles = static_cast<int32_t>(tiles);
+    a.err = d_err;
+    const int grid = static_cast<int>(std::min<int64_t>(tiles, resident));
+    if (restore) origami::restore_tma<MODE, D><<<grid, kThreads, smem, st>>>(a);
+    else origami::pack_tma<MODE, D><<<grid, kThreads, smem, st>>>(a);
+    rc = after_launch(restore ? "restore_tma launch" : "pack_tma launch");
+    if (rc) return rc;
+  }
+  return ORIGAMI_OK;
 }
 
 template <int MODE>
-int32_t launch_tma_by_dim(bool restore, int64_t D, const origami_paged_kv* cache, const PagedGeom& g,
-                          const int64_t* ids, int64_t T, const origami_planes* pl, const int64_t* off, int64_t S,
-                          uint8_t* packed, uint32_t* err, cudaStream_t st) {
+int32_t launch_tma_by_dim(bool restore, int64_t D, const origami_paged_kv* cache, const PagedGeom& g, const Job* jobs,
+                          int num_jobs, int64_t T, const int64_t* off, int64_t S, uint8_t* packed, int64_t job_stride,
+                          uint32_t* err, cudaStream_t st) {
   switch (D) {
-    case 64: return launch_tma<MODE, 64>(restore, cache, g, ids, T, pl, off, S, packed, err, st);
-    case 128: return launch_tma<MODE, 128>(restore, cache, g, ids, T, pl, off, S, packed, err, st);
-    default: return launch_tma<MODE, 256>(restore, cache, g, ids, T, pl, off, S, packed, err, st);
+    case 64: return launch_tma<MODE, 64>(restore, cache, g, jobs, num_jobs, T, off, S, packed, job_stride, err, st);
+    case 128: return launch_tma<MODE, 128>(restore, cache, g, jobs, num_jobs, T, off, S, packed, job_stride, err, st);
+    default: return launch_tma<MODE, 256>(restore, cache, g, jobs, num_jobs, T, off, S, packed, job_stride, err, st);
   }
 }
 
-int32_t layer_common(bool restore, const origami_paged_kv* cache, const int64_t* d_block_ids,
-                     int64_t num_block_ids, int64_t T, const origami_planes* planes,
-                     const origami_chunk_table* table, uint8_t* d_packed, int64_t packed_bytes,
-                     uint32_t* d_err, cudaStream_t st) {
+// Fused layer ops over `num_jobs` jobs sharing one chunk table and cache geometry; job j's
+// packed bytes start at d_packed + j * job_stride.
+int32_t layer_common(bool restore, const origami_paged_kv* cache, const Job* jobs, int num_jobs, int64_t T,
+                     const origami_planes* planes, const origami_chunk_table* table, uint8_t* d_packed,
+                     int64_t packed_bytes, int64_t job_stride, uint32_t* d_err, cudaStream_t st) {
+  if (cache == nullptr) return fail(ORIGAMI_ERR_INVALID, "kv cache descriptor is null");
+  if (num_jobs <= 0 || jobs == nullptr) return fail(ORIGAMI_ERR_INVALID, "at least one job is required");
+  origami_paged_kv geom = *cache;
+  geom.d_data = jobs[0].rows;
   PagedGeom g{};
-  int32_t rc = validate_cache(cache, g);
+  int32_t rc = validate_cache(&geom, g);
   if (rc) return rc;
   rc = validate_planes(planes);
   if (rc) return rc;
@@ -497,9 +520,13 @@ int32_t layer_common(bool restore, const origami_paged_kv* cache, const int64_t*
   if (T > 0x7FFFFFFF || cache->block_size > 0x7FFFFFFF)
     return fail(ORIGAMI_ERR_UNSUPPORTED, "num_tokens and block_size must be below 2^31");
   const int64_t need_blocks = (T + cache->block_size - 1) / cache->block_size;
-  if (d_block_ids == nullptr || num_block_ids < need_blocks)
-    return fail(ORIGAMI_ERR_INVALID, "block table has %lld ids, %lld tokens need %lld", (long long)num_block_ids,
-                (long long)T, (long long)need_blocks);
+  for (int j = 0; j < num_jobs; ++j) {
+    if (jobs[j].rows == nullptr || !aligned(jobs[j].rows, 16))
+      return fail(ORIGAMI_ERR_INVALID, "job %d: kv cache must be non-null and 16-byte aligned", j);
+    if (jobs[j].ids == nullptr || jobs[j].num_ids < need_blocks)
+      return fail(ORIGAMI_ERR_INVALID, "block table of job %d has %lld ids, %lld tokens need %lld", j,
+                  (long long)jobs[j].num_ids, (long long)T, (long long)need_blocks);
+  }
   const int64_t S = table->num_specs;
   if (S <= 0 || S > 32767) return fail(ORIGAMI_ERR_INVALID, "num_specs must be 1..32767");
   if (table->d_specs == nullptr || table->d_offsets == nullptr || table->h_offsets == nullptr)
@@ -521,37 +548,38 @@ int32_t layer_common(bool restore, const origami_paged_kv* cache, const int64_t*
       return fail(ORIGAMI_ERR_INVALID, "chunk %lld: offsets give %lld bytes, expected %lld", (long long)k,
                   (long long)(off[k + 1] - off[k]), (long long)expect);
   }
-  if (off[nchunks] > packed_bytes)
-    return fail(ORIGAMI_ERR_INVALID, "packed buffer holds %lld bytes, chunk table needs %lld", (long long)packed_bytes,
-                (long long)off[nchunks]);
+  if (num_jobs > 1 && (job_stride < off[nchunks] || job_stride % 16 != 0))
+    return fail(ORIGAMI_ERR_INVALID, "job stride %lld must be a multiple of 16 holding %lld bytes",
+                (long long)job_stride, (long long)off[nchunks]);
+  const int64_t extent = static_cast<int64_t>(num_jobs - 1) * job_stride + off[nchunks];
+  if (extent > packed_bytes)
+    return fail(ORIGAMI_ERR_INVALID, "packed buffer holds %lld bytes, the chunk table needs %lld",
+                (long long)packed_bytes, (long long)extent);
   if (d_packed == nullptr || !aligned(d_packed, 16)) return fail(ORIGAMI_ERR_INVALID, "packed buffer must be 16-byte aligned");
+  if (num_jobs == 1) job_stride = (off[nchunks] + 15) & ~static_cast<int64_t>(15);
 
   const int mode = classify_planes(*planes);
   if (tma_eligible(mode, specs, off, planes, T, H, D, d_packed)) {
     switch (mode) {
       case origami::kModeByte2:
-        return launch_tma_by_dim<origami::kModeByte2>(restore, D, cache, g, d_block_ids, T, planes, off, S, d_packed,
-                                                      d_err, st);
+        return launch_tma_by_dim<origami::kModeByte2>(restore, D, &geom, g, jobs, num_jobs, T, off, S, d_packed,
+                                                      job_stride, d_err, st);
       case origami::kModeBf16Bits:
-        return launch_tma_by_dim<origami::kModeBf16Bits>(restore, D, cache, g, d_block_ids, T, planes, off, S,
-                                                         d_packed, d_err, st);
+        return launch_tma_by_dim<origami::kModeBf16Bits>(restore, D, &geom, g, jobs, num_jobs, T, off, S, d_packed,
+                                                         job_stride, d_err, st);
       default:
-        return launch_tma_by_dim<origami::kModeFp16Bits>(restore, D, cache, g, d_block_ids, T, planes, off, S,
-                                                         d_packed, d_err, st);
+        return launch_tma_by_dim<origami::kModeFp16Bits>(restore, D, &geom, g, jobs, num_jobs, T, off, S, d_packed,
+                                                         job_stride, d_err, st);
     }
   }
 
   TileArgs a{};
-  a.rows = cache->d_data;
   a.kv_stride = g.kv_stride;
   a.block_stride = g.block_stride;
   a.token_stride = g.token_stride;
   a.head_stride = g.head_stride;
   a.block_size = cache->block_size;
   a.num_blocks = cache->num_blocks;
-  a.block_ids = d_block_ids;
-  a.packed = d_packed;
-  a.packed_bytes = packed_bytes;
   a.specs = table->d_specs;
   a.offsets = table->d_offsets;
   a.chunk_bits = nullptr;
@@ -570,7 +598,15 @@ int32_t layer_common(bool restore, const origami_paged_kv* cache, const int64_t*
   a.err = d_err;
   const size_t smem = layout_tile_smem(a, 2, restore, planes->bits);
   if (smem > 227 * 1024) return fail(ORIGAMI_ERR_UNSUPPORTED, "tile needs %zu bytes of shared memory", smem);
-  return dispatch_tiles(restore, 2, mode, a, smem, st);
+  for (int j = 0; j < num_jobs; ++j) {
+    a.rows = jobs[j].rows;
+    a.block_ids = jobs[j].ids;
+    a.packed = d_packed + static_cast<int64_t>(j) * job_stride;
+    a.packed_bytes = packed_bytes - static_cast<int64_t>(j) * job_stride;
+    rc = dispatch_tiles(restore, 2, mode, a, smem, st);
+    if (rc) return rc;
+  }
+  return ORIGAMI_OK;
 }
 
 int32_t slab_geometry(const origami_paged_kv* cache, int64_t num_block_ids, int64_t bytes, int64_t& slab,
@@ -638,17 +674,50 @@ int32_t origami_pack_layer_from_paged(const origami_paged_kv* cache, const int64
                                       int64_t num_block_ids, int64_t num_tokens, const origami_planes* planes,
                                       const origami_chunk_table* table, uint8_t* d_packed, int64_t packed_bytes,
                                       uint32_t* d_error_count, origami_stream_t stream) {
-  return layer_common(false, cache, d_block_ids, num_block_ids, num_tokens, planes, table, d_packed, packed_bytes,
-                      d_error_count, reinterpret_cast<cudaStream_t>(stream));
+  if (cache == nullptr) return fail(ORIGAMI_ERR_INVALID, "kv cache is null");
+  const Job job{cache->d_data, d_block_ids, num_block_ids};
+  return layer_common(false, cache, &job, 1, num_tokens, planes, table, d_packed, packed_bytes, 0, d_error_count,
+                      reinterpret_cast<cudaStream_t>(stream));
 }
 
 int32_t origami_restore_layer_to_paged(const uint8_t* d_packed, int64_t packed_bytes, const origami_planes* planes,
                                        const origami_chunk_table* table, const origami_paged_kv* cache,
                                        const int64_t* d_block_ids, int64_t num_block_ids, int64_t num_tokens,
                                        uint32_t* d_error_count, origami_stream_t stream) {
-  return layer_common(true, cache, d_block_ids, num_block_ids, num_tokens, planes, table,
-                      const_cast<uint8_t*>(d_packed), packed_bytes, d_error_count,
-                      reinterpret_cast<cudaStream_t>(stream));
+  if (cache == nullptr) return fail(ORIGAMI_ERR_INVALID, "kv cache is null");
+  const Job job{cache->d_data, d_block_ids, num_block_ids};
+  return layer_common(true, cache, &job, 1, num_tokens, planes, table, const_cast<uint8_t*>(d_packed), packed_bytes,
+                      0, d_error_count, reinterpret_cast<cudaStream_t>(stream));
+}
+
+static int32_t jobs_from(const origami_layer_job* jobs, int32_t n, std::vector<Job>& out) {
+  if (jobs == nullptr || n <= 0) return fail(ORIGAMI_ERR_INVALID, "at least one job is required");
+  out.resize(static_cast<size_t>(n));
+  for (int32_t j = 0; j < n; ++j) out[j] = Job{jobs[j].d_kv_cache, jobs[j].d_block_ids, jobs[j].num_block_ids};
+  return ORIGAMI_OK;
+}
+
+int32_t origami_pack_layers_from_paged(const origami_paged_kv* cache, const origami_layer_job* jobs, int32_t num_jobs,
+                                       int64_t num_tokens, const origami_planes* planes,
+                                       const origami_chunk_table* table, uint8_t* d_packed, int64_t packed_bytes,
+                                       int64_t job_stride, uint32_t* d_error_count, origami_stream_t stream) {
+  std::vector<Job> js;
+  const int32_t rc = jobs_from(jobs, num_jobs, js);
+  if (rc) return rc;
+  return layer_common(false, cache, js.data(), num_jobs, num_tokens, planes, table, d_packed, packed_bytes,
+                      job_stride, d_error_count, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int32_t origami_restore_layers_to_paged(const uint8_t* d_packed, int64_t packed_bytes, int64_t job_stride,
+                                        const origami_planes* planes, const origami_chunk_table* table,
+                                        const origami_paged_kv* cache, const origami_layer_job* jobs,
+                                        int32_t num_jobs, int64_t num_tokens, uint32_t* d_error_count,
+                                        origami_stream_t stream) {
+  std::vector<Job> js;
+  const int32_t rc = jobs_from(jobs, num_jobs, js);
+  if (rc) return rc;
+  return layer_common(true, cache, js.data(), num_jobs, num_tokens, planes, table, const_cast<uint8_t*>(d_packed),
+                      packed_bytes, job_stride, d_error_count, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int32_t origami_gather_blocks(const origami_paged_kv* cache, const int64_t* d_block_ids, int64_t num_block_ids,

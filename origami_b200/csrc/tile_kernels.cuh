@@ -566,14 +566,19 @@ __global__ void __launch_bounds__(kThreads) pack_tiles(const TileArgs args) {
       const int64_t nsrc = static_cast<int64_t>(tc.n) * pm[c].c;
       const uint32_t* src = reinterpret_cast<const uint32_t*>(pbase + c * rs);
       const int64_t rel = V * 128 - B;  // source bit of the vector's first bit
-      if ((B & 31) == 0 && rel >= 0 && rel + 128 <= nsrc && V * 128 + 128 <= E) {
-        // fully owned, word aligned vector made of source bits only
+      if (rel >= 0 && rel + 128 <= nsrc && V * 128 + 128 <= E) {
+        // fully owned vector made of source bits only: whole 16-byte store, the run's
+        // bit offset applied with funnel shifts (src[q + 4] < nsrc when r > 0)
         const int q = static_cast<int>(rel >> 5);
+        const int r = static_cast<int>(rel & 31);
         uint4 w;
-        if ((q & 3) == 0) {
-          w = *reinterpret_cast<const uint4*>(src + q);
+        if (r == 0) {
+          if ((q & 3) == 0) w = *reinterpret_cast<const uint4*>(src + q);
+          else w = make_uint4(src[q], src[q + 1], src[q + 2], src[q + 3]);
         } else {
-          w = make_uint4(src[q], src[q + 1], src[q + 2], src[q + 3]);
+          const uint32_t s0 = src[q], s1 = src[q + 1], s2 = src[q + 2], s3 = src[q + 3], s4 = src[q + 4];
+          w = make_uint4(__funnelshift_r(s0, s1, r), __funnelshift_r(s1, s2, r), __funnelshift_r(s2, s3, r),
+                         __funnelshift_r(s3, s4, r));
         }
         st_global_cs16(dst32 + 4 * V, w);
       } else {

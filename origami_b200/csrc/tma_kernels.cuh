@@ -27,15 +27,18 @@ namespace origami {
 
 constexpr uint32_t kWaitTimeoutFlag = 0x80000000u;
 constexpr int kMaxMaps = 2 * 3;  // K and V x at most 3 planes (the presets)
+constexpr int kMaxJobs = 128;    // jobs (layers / requests) per launch
 
+// Jobs share the chunk table and cache geometry; job j's packed runs are at coordinate
+// j of the 3rd tensor-map dimension, its rows in rows[j] through block_ids[j].
 struct TmaArgs {
-  CUtensorMap maps[kMaxMaps];  // component q = kv * P + p
-  void* rows;
+  CUtensorMap maps[kMaxMaps];  // component q = kv * P + p: {T*bits/8, H*D, jobs}
+  void* rows[kMaxJobs];
+  const int64_t* block_ids[kMaxJobs];
   int64_t kv_stride, block_stride, token_stride, head_stride;
   int64_t block_size, num_blocks;
-  const int64_t* block_ids;
   int64_t T;
-  int32_t H, tiles_per_head, num_tiles;
+  int32_t H, tiles_per_head, tiles_per_job, num_tiles;
   uint32_t* err;
 };
 
@@ -63,19 +66,20 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   return false;
 }
 
-__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int32_t x, int32_t y,
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, int32_t x, int32_t y, int32_t z,
                                             uint64_t* bar) {
   asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::"r"(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];\n" ::"r"(
           smem_u32(smem_dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
       : "memory");
 }
 
-__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, int32_t x, int32_t y, const void* smem_src) {
-  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%1, %2}], [%3];\n" ::"l"(
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, int32_t x, int32_t y, int32_t z,
+                                             const void* smem_src) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3}], [%4];\n" ::"l"(
                    reinterpret_cast<uint64_t>(map)),
-               "r"(x), "r"(y), "r"(smem_u32(smem_src))
+               "r"(x), "r"(y), "r"(z), "r"(smem_u32(smem_src))
                : "memory");
 }
 
@@ -88,7 +92,7 @@ __device__ __forceinline__ void fence_async_shared() { asm volatile("fence.proxy
 __device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory"); }
 
 struct TmaTile {
-  int kv, h;
+  int job, kv, h;
   int64_t t0;
   int n;
 };
@@ -96,8 +100,10 @@ struct TmaTile {
 template <int TT>
 __device__ __forceinline__ TmaTile tma_tile(const TmaArgs& a, int tile) {
   TmaTile t;
-  const int tt = tile % a.tiles_per_head;
-  const int rest = tile / a.tiles_per_head;
+  t.job = tile / a.tiles_per_job;
+  const int in_job = tile - t.job * a.tiles_per_job;
+  const int tt = in_job % a.tiles_per_head;
+  const int rest = in_job / a.tiles_per_head;
   t.h = rest % a.H;
   t.kv = rest / a.H;
   t.t0 = static_cast<int64_t>(tt) * TT;
@@ -116,7 +122,7 @@ __device__ __forceinline__ void tma_rowoff(const TmaArgs& a, const TmaTile& t, i
     }
     const int32_t tg = static_cast<int32_t>(t.t0) + i;
     const int32_t bi = tg / bs;
-    const int64_t blk = a.block_ids[bi];
+    const int64_t blk = a.block_ids[t.job][bi];
     if (blk < 0 || blk >= a.num_blocks) {
       rowoff[i] = -1;
       if (a.err) atomicAdd(a.err, 1u);
@@ -181,8 +187,8 @@ __global__ void __launch_bounds__(kThreads) restore_tma(const __grid_constant__ 
       mbar_expect_tx(&bars[s], G::in_bytes);
 #pragma unroll
       for (int p = 0; p < G::P; ++p) {
-        tma_load_2d(smem + s * G::stage_bytes + G::plane_off(p), &args.maps[t.kv * G::P + p],
-                    static_cast<int32_t>(t.t0 * G::bits(p) / 8), t.h * D, &bars[s]);
+        tma_load_3d(smem + s * G::stage_bytes + G::plane_off(p), &args.maps[t.kv * G::P + p],
+                    static_cast<int32_t>(t.t0 * G::bits(p) / 8), t.h * D, t.job, &bars[s]);
       }
     }
     tma_rowoff<G::TT>(args, t, reinterpret_cast<int64_t*>(smem + s * G::stage_bytes + G::in_bytes));
@@ -193,7 +199,6 @@ __global__ void __launch_bounds__(kThreads) restore_tma(const __grid_constant__ 
   uint32_t phases = 0u;  // bit s = parity to wait for on stage s
   const int a = tid % G::A;
   const int o = tid / G::A;
-  uint8_t* rows = static_cast<uint8_t*>(args.rows);
 
   for (int j = 0; tile < args.num_tiles; ++j, tile += gridDim.x) {
     const int s = j & 1;
@@ -208,6 +213,7 @@ __global__ void __launch_bounds__(kThreads) restore_tma(const __grid_constant__ 
     }
     phases ^= 1u << s;
     const TmaTile t = tma_tile<G::TT>(args, tile);
+    uint8_t* rows = static_cast<uint8_t*>(args.rows[t.job]);
 
     // Phase B: 8 tokens x 8 channels per thread, planes merged in registers.
     uint32_t out[8][4];
@@ -306,11 +312,11 @@ __global__ void __launch_bounds__(kThreads) pack_tma(const __grid_constant__ Tma
   uint8_t* smem = tma_smem + ((128 - (smem_u32(tma_smem) & 127)) & 127);
   uint8_t* out_sm = smem + 2 * PG::stage_bytes;
   const int tid = threadIdx.x;
-  const uint8_t* rows = static_cast<const uint8_t*>(args.rows);
 
   // Gather a tile's token rows with cp.async (8-channel chunks rotated by token octet).
   auto gather = [&](int s, int tile) {
     const TmaTile t = tma_tile<G::TT>(args, tile);
+    const uint8_t* rows = static_cast<const uint8_t*>(args.rows[t.job]);
     uint8_t* sb = smem + s * PG::stage_bytes;
     int64_t* rowoff = reinterpret_cast<int64_t*>(sb + PG::rows_bytes);
     tma_rowoff<G::TT>(args, t, rowoff);
@@ -400,7 +406,7 @@ __global__ void __launch_bounds__(kThreads) pack_tma(const __grid_constant__ Tma
     if (tid == 0) {
 #pragma unroll
       for (int p = 0; p < G::P; ++p) {
-        tma_store_2d(&args.maps[t.kv * G::P + p], static_cast<int32_t>(t.t0 * G::bits(p) / 8), t.h * D,
+        tma_store_3d(&args.maps[t.kv * G::P + p], static_cast<int32_t>(t.t0 * G::bits(p) / 8), t.h * D, t.job,
                      out_sm + G::plane_off(p));
       }
       tma_store_commit();

@@ -125,6 +125,65 @@ def restore_layer(packed: torch.Tensor, fmt: LayerFormat, kv_layer: torch.Tensor
     _lib.check(rc, "origami_restore_layer_to_paged")
 
 
+def _jobs(kv_layers, block_ids, device) -> tuple[_lib.PagedKV, ctypes.Array, list]:
+    if len(kv_layers) != len(block_ids) or not kv_layers:
+        raise ValueError("one block table per job is required")
+    descs = [paged_desc(t) for t in kv_layers]
+    d0 = descs[0]
+    for d in descs[1:]:
+        if (d.layout, d.num_blocks, d.block_size, d.num_heads, d.head_dim) != (
+                d0.layout, d0.num_blocks, d0.block_size, d0.num_heads, d0.head_dim):
+            raise ValueError("batched jobs must share the cache geometry")
+    ids = [block_ids_tensor(b, device) for b in block_ids]
+    arr = (_lib.LayerJob * len(descs))(*[_lib.LayerJob(d.d_data, i.data_ptr(), i.numel()) for d, i in zip(descs, ids)])
+    return d0, arr, ids
+
+
+def job_stride(fmt: LayerFormat) -> int:
+    """Byte stride of consecutive jobs in a batched packed buffer (16-byte multiple)."""
+    return (fmt.packed_bytes + 15) // 16 * 16
+
+
+def alloc_jobs_packed(fmt: LayerFormat, num_jobs: int, device) -> torch.Tensor:
+    return torch.empty((num_jobs * job_stride(fmt),), dtype=torch.uint8, device=device)
+
+
+def restore_layers(packed: torch.Tensor, fmt: LayerFormat, kv_layers, block_ids, *,
+                   stream: torch.cuda.Stream | None = None, error_count: torch.Tensor | None = None) -> None:
+    """Restore len(kv_layers) jobs (layers / requests sharing fmt) in as few launches as
+    possible; job j's chunks start at packed[j * job_stride(fmt)]."""
+    device = kv_layers[0].device
+    d0, arr, _ids = _jobs(kv_layers, block_ids, device)
+    if d0.num_heads != fmt.num_heads or d0.head_dim != fmt.head_dim:
+        raise ValueError("layer format heads / head_dim do not match the cache")
+    pl = planes_desc(fmt)
+    tab = _table(fmt, device)
+    with torch.cuda.device(device):
+        rc = _lib.lib().origami_restore_layers_to_paged(
+            packed.data_ptr(), packed.numel(), job_stride(fmt), ctypes.byref(pl), ctypes.byref(tab), ctypes.byref(d0),
+            arr, len(arr), fmt.num_tokens, error_count.data_ptr() if error_count is not None else None,
+            _stream_handle(stream, device))
+    _lib.check(rc, "origami_restore_layers_to_paged")
+
+
+def pack_layers(kv_layers, block_ids, fmt: LayerFormat, out: torch.Tensor, *,
+                stream: torch.cuda.Stream | None = None, error_count: torch.Tensor | None = None) -> torch.Tensor:
+    """Pack len(kv_layers) jobs sharing fmt into `out` (job j at j * job_stride(fmt))."""
+    device = kv_layers[0].device
+    d0, arr, _ids = _jobs(kv_layers, block_ids, device)
+    if d0.num_heads != fmt.num_heads or d0.head_dim != fmt.head_dim:
+        raise ValueError("layer format heads / head_dim do not match the cache")
+    pl = planes_desc(fmt)
+    tab = _table(fmt, device)
+    with torch.cuda.device(device):
+        rc = _lib.lib().origami_pack_layers_from_paged(
+            ctypes.byref(d0), arr, len(arr), fmt.num_tokens, ctypes.byref(pl), ctypes.byref(tab), out.data_ptr(),
+            out.numel(), job_stride(fmt), error_count.data_ptr() if error_count is not None else None,
+            _stream_handle(stream, device))
+    _lib.check(rc, "origami_pack_layers_from_paged")
+    return out
+
+
 def gather_blocks(kv_layer: torch.Tensor, block_ids, *, out: torch.Tensor | None = None,
                   stream: torch.cuda.Stream | None = None, error_count: torch.Tensor | None = None) -> torch.Tensor:
     """index_select along the block dimension; returns the gathered blocks."""

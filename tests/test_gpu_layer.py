@@ -138,3 +138,34 @@ def test_raw_gather_scatter_match_torch(cuda, kv_first):
     expect = torch.zeros_like(d)
     expect.index_copy_(dim, ids.to(cuda), want)
     assert torch.equal(fresh.view(torch.int16), expect.view(torch.int16))
+
+
+@pytest.mark.parametrize("planes", [BYTE_PLANES, BF16_BIT_PLANES, FP16_BIT_PLANES, ODD_PLANES], ids=lambda p: p.name)
+@pytest.mark.parametrize("T, jobs", [(1024, 5), (1000, 3), (256, 131)])
+def test_batched_jobs_match_per_job(oracle, cuda, planes, T, jobs):
+    """Batched pack/restore over several layers (own caches, own block tables) gives the
+    per-job results and the oracle's bytes; 131 jobs span two persistent launches."""
+    from origami_b200.layer import alloc_jobs_packed, job_stride, pack_layers, restore_layers
+
+    bs, H, D = 16, 2, 128
+    fmt = LayerFormat(T, H, D, planes, 1 << 16, 1 << 16, 1 << 16)
+    caches, ids = [], []
+    for j in range(jobs):
+        c, i = make_cache(T, bs, H, D, True, seed=1000 + j)
+        caches.append(c.to(cuda))
+        ids.append(i)
+    arena = alloc_jobs_packed(fmt, jobs, cuda)
+    arena.fill_(0x5A)
+    pack_layers(caches, ids, fmt, arena)
+    stride = job_stride(fmt)
+    got = arena.cpu().numpy()
+    for j in (0, jobs // 2, jobs - 1):
+        want, _ = oracle.pack_layer(u16(caches[j].cpu()), 0, ids[j].numpy(), T, planes.shifts, planes.bits, fmt.specs)
+        np.testing.assert_array_equal(got[j * stride:j * stride + fmt.packed_bytes], want, err_msg=f"job {j}")
+    fresh = [torch.zeros_like(c) for c in caches]
+    restore_layers(arena, fmt, fresh, ids)
+    t = torch.arange(T)
+    for j in range(jobs):
+        blk = ids[j][t // bs]
+        assert torch.equal(fresh[j].cpu()[:, blk, t % bs].view(torch.int16),
+                           caches[j].cpu()[:, blk, t % bs].view(torch.int16)), j
