@@ -48,6 +48,7 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=0, help="layers (default: 32 for C2, 4 for C3, 8 for C5)")
     ap.add_argument("--config", choices=("C2", "C3", "C5"), default="C2", help="workload (C2 is the headline)")
     ap.add_argument("--chunk-bytes", type=int, default=1 << 20, help="codec chunk size (min = target = max)")
+    ap.add_argument("--tokens", type=int, default=0, help="C2 only: tokens per request (default 32768)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="bound on the CPU baseline sample")
@@ -189,7 +190,7 @@ class Workload:
     """
 
     def __init__(self, config: str, rank: int, world: int, layers: int, planes_name: str, device,
-                 chunk_bytes: int = 1 << 20):
+                 chunk_bytes: int = 1 << 20, tokens_override: int = 0):
         import torch
 
         from origami_b200 import LayerFormat, plane_spec, workloads
@@ -198,7 +199,7 @@ class Workload:
         self.config = config
         if config == "C2":
             cfg = workloads.C2
-            tokens = [cfg.tokens[0]] * world
+            tokens = [tokens_override or cfg.tokens[0]] * world
             self.scaling = "weak"
         elif config == "C3":
             cfg = workloads.c3_config()
@@ -273,7 +274,7 @@ class Workload:
 
         n = 0
         for fmt, jobs, _ in self.groups:
-            n += (len(jobs) + 127) // 128 if fused_kernel_name(fmt).endswith("tma") else len(jobs)
+            n += len(jobs) if fused_kernel_name(fmt).endswith("tiles") else (len(jobs) + 127) // 128
         return n
 
     @property
@@ -305,7 +306,7 @@ def run_origami(args, rank, world, local):
 
     device = torch.device("cuda", local)
     layers = args.layers if args.layers else {"C2": 32, "C3": 4, "C5": 8}[args.config]
-    wl = Workload(args.config, rank, world, layers, args.planes, device, args.chunk_bytes)
+    wl = Workload(args.config, rank, world, layers, args.planes, device, args.chunk_bytes, args.tokens)
     stream = torch.cuda.current_stream(device)
     err = torch.zeros(1, dtype=torch.int32, device=device)
 
@@ -398,7 +399,7 @@ def run_origami(args, rank, world, local):
     k_restore = "/".join(sorted(kinds))
     k_pack = "/".join(sorted({fused_kernel_name(f, False) for f in wl.fmts}))
     workload_name = (f"C2_restore_T{wl.tokens[0]}_H{wl.heads}_D{wl.cfg.head_dim}_{wl.planes.name}"
-                     if args.config == "C2" and args.chunk_bytes == 1 << 20 else None)
+                     if args.config == "C2" and args.chunk_bytes == 1 << 20 and not args.tokens else None)
     roof_restore = {"kernel": k_restore, "bound": "hbm", "achieved": round(achieved_restore, 1), "peak": peak,
                     "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved_restore / peak, 4),
                     "traffic": profiled_traffic(k_restore, workload_name) if workload_name else None,

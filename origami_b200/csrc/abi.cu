@@ -15,6 +15,7 @@
 #include "linear_kernels.cuh"
 #include "tile_kernels.cuh"
 #include "tma_kernels.cuh"
+#include "bulk_kernels.cuh"
 
 namespace {
 
@@ -137,7 +138,7 @@ size_t layout_tile_smem(TileArgs& a, int elem, bool restore, const int* plane_bi
   size_t planes_bytes = 0;
   for (int p = 0; p < P; ++p) planes_bytes += static_cast<size_t>(D) * origami::run_stride(TT, plane_bits[p], restore);
   const size_t rows_bytes = static_cast<size_t>(TT) * D * elem;
-  return off + std::max(planes_bytes, rows_bytes);
+  return off + std::max(planes_bytes, rows_bytes) + 32;  // + slack for window64 / words5 over-reads
 }
 
 int classify_planes(const origami_planes& pl) {
@@ -498,6 +499,88 @@ int32_t launch_tma_by_dim(bool restore, int64_t D, const origami_paged_kv* cache
   }
 }
 
+// Contiguous canonical format (see bulk_kernels.cuh): runs at computable bit offsets,
+// any token count with T * bits a multiple of 8.
+bool bulk_eligible(int mode, const std::vector<Spec>& specs, const int64_t* off, const origami_planes* pl, int64_t T,
+                   int64_t D, const uint8_t* packed, int num_jobs, int64_t job_stride) {
+  if (mode == origami::kModeGeneric) return false;
+  if (D != 64 && D != 128 && D != 256) return false;
+  if (!aligned(packed, 16) || (num_jobs > 1 && job_stride % 16 != 0)) return false;
+  const int64_t S = static_cast<int64_t>(specs.size());
+  const int P = pl->num_planes;
+  for (int q = 0; q < 2 * P; ++q) {
+    const int b = pl->bits[q % P];
+    if ((T * b) % 8 != 0) return false;
+    const int64_t run = T * b / 8;
+    for (int64_t s = 0; s < S; ++s)
+      if (off[q * S + s] != off[q * S] + (specs[s].h0 * D + specs[s].c0) * run) return false;
+  }
+  return true;
+}
+
+template <int MODE, int D>
+int32_t launch_bulk(bool restore, const origami_paged_kv* cache, const PagedGeom& g, const Job* jobs, int num_jobs,
+                    int64_t T, const int64_t* off, int64_t S, uint8_t* packed, int64_t packed_bytes, int64_t job_stride,
+                    uint32_t* d_err, cudaStream_t st) {
+  using G = origami::TmaGeo<MODE, D>;
+  const void* fn = restore ? reinterpret_cast<const void*>(&origami::restore_bulk<MODE, D>)
+                           : reinterpret_cast<const void*>(&origami::pack_bulk<MODE, D>);
+  const int smem = restore ? origami::BulkGeo<MODE, D>::smem_bytes : origami::PackBulkGeo<MODE, D>::smem_bytes;
+  int resident = 0;
+  int32_t rc = persistent_slots(fn, smem, resident);
+  if (rc) return rc;
+  const int32_t tiles_per_head = static_cast<int32_t>((T + G::TT - 1) / G::TT);
+  const int64_t tiles_per_job = 2 * cache->num_heads * tiles_per_head;
+  for (int j0 = 0; j0 < num_jobs; j0 += origami::kMaxJobs) {
+    const int nj = std::min(num_jobs - j0, origami::kMaxJobs);
+    origami::BulkArgs a{};
+    a.packed = packed + static_cast<int64_t>(j0) * job_stride;
+    a.job_stride = job_stride;
+    a.packed_bytes = packed_bytes - static_cast<int64_t>(j0) * job_stride;
+    for (int q = 0; q < 2 * G::P; ++q) a.comp_base[q] = off[q * S];
+    for (int j = 0; j < nj; ++j) {
+      a.rows[j] = jobs[j0 + j].rows;
+      a.block_ids[j] = jobs[j0 + j].ids;
+    }
+    a.kv_stride = g.kv_stride;
+    a.block_stride = g.block_stride;
+    a.token_stride = g.token_stride;
+    a.head_stride = g.head_stride;
+    a.block_size = cache->block_size;
+    a.num_blocks = cache->num_blocks;
+    a.T = T;
+    a.H = static_cast<int32_t>(cache->num_heads);
+    a.tiles_per_head = tiles_per_head;
+    const int64_t tiles = tiles_per_job * nj;
+    if (tiles > 0x7FFFFFFF) return fail(ORIGAMI_ERR_UNSUPPORTED, "too many tiles");
+    a.tiles_per_job = static_cast<int32_t>(tiles_per_job);
+    a.num_tiles = static_cast<int32_t>(tiles);
+    a.err = d_err;
+    const int grid = static_cast<int>(std::min<int64_t>(tiles, resident));
+    if (restore) origami::restore_bulk<MODE, D><<<grid, kThreads, smem, st>>>(a);
+    else origami::pack_bulk<MODE, D><<<grid, kThreads, smem, st>>>(a);
+    rc = after_launch(restore ? "restore_bulk launch" : "pack_bulk launch");
+    if (rc) return rc;
+  }
+  return ORIGAMI_OK;
+}
+
+template <int MODE>
+int32_t launch_bulk_by_dim(bool restore, int64_t D, const origami_paged_kv* cache, const PagedGeom& g, const Job* jobs,
+                           int num_jobs, int64_t T, const int64_t* off, int64_t S, uint8_t* packed,
+                           int64_t packed_bytes, int64_t job_stride, uint32_t* err, cudaStream_t st) {
+  switch (D) {
+    case 64:
+      return launch_bulk<MODE, 64>(restore, cache, g, jobs, num_jobs, T, off, S, packed, packed_bytes, job_stride, err, st);
+    case 128:
+      return launch_bulk<MODE, 128>(restore, cache, g, jobs, num_jobs, T, off, S, packed, packed_bytes, job_stride, err,
+                                    st);
+    default:
+      return launch_bulk<MODE, 256>(restore, cache, g, jobs, num_jobs, T, off, S, packed, packed_bytes, job_stride, err,
+                                    st);
+  }
+}
+
 // Fused layer ops over `num_jobs` jobs sharing one chunk table and cache geometry; job j's
 // packed bytes start at d_packed + j * job_stride.
 int32_t layer_common(bool restore, const origami_paged_kv* cache, const Job* jobs, int num_jobs, int64_t T,
@@ -570,6 +653,19 @@ int32_t layer_common(bool restore, const origami_paged_kv* cache, const Job* job
       default:
         return launch_tma_by_dim<origami::kModeFp16Bits>(restore, D, &geom, g, jobs, num_jobs, T, off, S, d_packed,
                                                          job_stride, d_err, st);
+    }
+  }
+  if (bulk_eligible(mode, specs, off, planes, T, D, d_packed, num_jobs, job_stride)) {
+    switch (mode) {
+      case origami::kModeByte2:
+        return launch_bulk_by_dim<origami::kModeByte2>(restore, D, &geom, g, jobs, num_jobs, T, off, S, d_packed,
+                                                       packed_bytes, job_stride, d_err, st);
+      case origami::kModeBf16Bits:
+        return launch_bulk_by_dim<origami::kModeBf16Bits>(restore, D, &geom, g, jobs, num_jobs, T, off, S, d_packed,
+                                                          packed_bytes, job_stride, d_err, st);
+      default:
+        return launch_bulk_by_dim<origami::kModeFp16Bits>(restore, D, &geom, g, jobs, num_jobs, T, off, S, d_packed,
+                                                          packed_bytes, job_stride, d_err, st);
     }
   }
 

@@ -44,6 +44,51 @@ __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.wait_group 0;\n" ::: "memory");
 }
 
+// ---------------------------------------------------------------------------
+// mbarriers and bulk (TMA) copies. Waits are bounded: a kernel whose wait runs out
+// flags kWaitTimeoutFlag in its error word instead of spinning forever.
+// ---------------------------------------------------------------------------
+constexpr uint32_t kWaitTimeoutFlag = 0x80000000u;
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+// Bounded wait for phase `parity` of an mbarrier; false when the bound ran out.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+  const uint32_t addr = smem_u32(bar);
+  for (uint32_t i = 0; i < (1u << 22); ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+
+__device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory"); }
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// 1-D bulk copy global -> shared (16-byte aligned addresses, size a multiple of 16),
+// completing `bytes` transactions on the mbarrier.
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+                   smem_u32(smem_dst)),
+               "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
 // Streaming 16-byte global store (data is not re-read by this kernel).
 __device__ __forceinline__ void st_global_cs16(void* p, uint4 v) {
   asm volatile("st.global.cs.v4.u32 [%0], {%1, %2, %3, %4};\n" ::"l"(p), "r"(v.x), "r"(v.y),
@@ -105,16 +150,35 @@ __device__ __forceinline__ void transpose8x8(uint32_t (&lo)[8], uint32_t (&hi)[8
 // ---------------------------------------------------------------------------
 
 // 64 bits of a 16-byte-aligned shared-memory row starting at bit `bitpos`.
+// Two aligned 64-bit shared loads cover words wi..wi+2 (fewer bank conflicts than three
+// 32-bit loads at a 2-word lane stride); reads at most 4 bytes past word wi + 2.
 __device__ __forceinline__ void window64(const uint8_t* row, int bitpos, uint32_t& v0,
                                          uint32_t& v1) {
-  const uint32_t* w = reinterpret_cast<const uint32_t*>(row);
   const int wi = bitpos >> 5;
   const int sh = bitpos & 31;
-  const uint32_t w0 = w[wi];
-  const uint32_t w1 = w[wi + 1];
-  const uint32_t w2 = w[wi + 2];
+  const uint2* p = reinterpret_cast<const uint2*>(row) + (wi >> 1);
+  const uint2 a = p[0];
+  const uint2 b = p[1];
+  const bool odd = (wi & 1) != 0;
+  const uint32_t w0 = odd ? a.y : a.x;
+  const uint32_t w1 = odd ? b.x : a.y;
+  const uint32_t w2 = odd ? b.y : b.x;
   v0 = __funnelshift_r(w0, w1, sh);
   v1 = __funnelshift_r(w1, w2, sh);
+}
+
+// Words q..q+4 of a 16-byte aligned shared row from two aligned 16-byte loads; reads at
+// most 12 bytes past word q + 4.
+__device__ __forceinline__ void words5(const uint32_t* src, int q, uint32_t (&s)[5]) {
+  const int qa = q & ~3;
+  const int d = q & 3;
+  const uint4 x = *reinterpret_cast<const uint4*>(src + qa);
+  const uint4 y = *reinterpret_cast<const uint4*>(src + qa + 4);
+  const uint32_t w[8] = {x.x, x.y, x.z, x.w, y.x, y.y, y.z, y.w};
+#pragma unroll
+  for (int k = 0; k < 5; ++k) {
+    s[k] = d == 0 ? w[k] : d == 1 ? w[k + 1] : d == 2 ? w[k + 2] : w[k + 3];
+  }
 }
 
 // Spread 8 consecutive `bits`-wide symbols of a 64-bit window into 8 bytes.

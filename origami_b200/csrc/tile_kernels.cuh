@@ -231,38 +231,53 @@ __global__ void __launch_bounds__(kThreads) restore_tiles(const TileArgs args) {
   }
   __syncthreads();
 
-  // Phase A: stage the covering 16-byte words of every run.
-#pragma unroll 1
-  for (int p = 0; p < P; ++p) {
-    const int rs = plane_stride<MODE, DT>(args, g, p, true);
-    const int W = rs >> 4;
-    const int cnt = D * W;
-    uint8_t* pbase = data + plane_base<MODE, DT>(args, g, p, true);
-    const RowMeta* pm = meta + p * D;
-    for (int i = tid; i < cnt; i += kThreads) {
-      const int c = i / W;
-      const int w = i - c * W;
-      const int64_t ma = pm[c].a;
-      uint8_t* dst = pbase + c * rs + w * 16;
-      if (ma < 0) {
-        *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+  // Phase A: stage the covering 16-byte words of every run, one bulk (TMA) copy per run
+  // row; rows no chunk covers are zero-filled, words past the buffer end read bytewise.
+  __shared__ __align__(8) uint64_t bar;
+  if (tid == 0) {
+    mbar_init(&bar, kThreads);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  {
+    uint32_t my_bytes = 0;  // announced before any of this thread's copies can complete
+    for (int r = tid; r < P * D; r += kThreads) {
+      const RowMeta m = meta[r];
+      if (m.a < 0) continue;
+      const int64_t full = min64(m.b, (args.packed_bytes - m.a) >> 4);
+      if (full > 0) my_bytes += static_cast<uint32_t>(full) * 16u;
+    }
+    mbar_expect_tx(&bar, my_bytes);
+    for (int r = tid; r < P * D; r += kThreads) {
+      const int p = r / D;
+      const int c = r - p * D;
+      const int rs = plane_stride<MODE, DT>(args, g, p, true);
+      uint8_t* row = data + plane_base<MODE, DT>(args, g, p, true) + c * rs;
+      const RowMeta m = meta[r];
+      if (m.a < 0) {
+        for (int w = 0; w < (rs >> 4); ++w) *reinterpret_cast<uint4*>(row + 16 * w) = make_uint4(0u, 0u, 0u, 0u);
         continue;
       }
-      if (w >= pm[c].b) continue;
-      const int64_t gofs = ma + 16 * static_cast<int64_t>(w);
-      if (gofs + 16 <= args.packed_bytes) {
-        cp_async16(dst, args.packed + gofs);
-      } else {
+      const int64_t full = min64(m.b, (args.packed_bytes - m.a) >> 4);
+      if (full > 0) bulk_load(row, args.packed + m.a, static_cast<uint32_t>(full) * 16u, &bar);
+      for (int64_t w = max64(full, 0); w < m.b; ++w) {  // words straddling the buffer end
+        const int64_t gofs = m.a + 16 * w;
         uint32_t v[4] = {0u, 0u, 0u, 0u};
         for (int j = 0; j < 16; ++j) {
           if (gofs + j < args.packed_bytes) v[j >> 2] |= static_cast<uint32_t>(args.packed[gofs + j]) << (8 * (j & 3));
         }
-        *reinterpret_cast<uint4*>(dst) = make_uint4(v[0], v[1], v[2], v[3]);
+        *reinterpret_cast<uint4*>(row + 16 * w) = make_uint4(v[0], v[1], v[2], v[3]);
       }
     }
   }
-  cp_async_wait_all();
-  __syncthreads();
+  {
+    const bool ok = mbar_wait_bounded(&bar, 0);
+    if (__syncthreads_or(!ok)) {
+      if (tid == 0 && args.err) atomicOr(args.err, kWaitTimeoutFlag);
+      mbar_wait_bounded(&bar, 0);
+      return;
+    }
+  }
 
   // Phase B: 8 tokens x 8 channels per thread.
   const int A = g.A;
@@ -377,30 +392,25 @@ __global__ void __launch_bounds__(kThreads) restore_tiles(const TileArgs args) {
 // Pack: rows -> packed chunks
 // ---------------------------------------------------------------------------------------
 
-// One destination 32-bit word W of a run whose stream bits are [B, E) and whose first
-// nsrc bits come from `src` (a 16-byte aligned shared row; bits past nsrc are zero pad):
-// plain store when the run owns the whole word, otherwise a masked atomic clear + set of
-// the run's own bits (the neighbouring run owns the rest of the word).
-__device__ __forceinline__ void put_word(uint32_t* dst32, int64_t W, int64_t B, int64_t E, int64_t nsrc,
-                                         const uint32_t* src) {
-  const int64_t rel = W * 32 - B;
-  const int64_t nsw = (nsrc + 31) >> 5;
-  const int64_t q = rel >> 5;
-  const int r = static_cast<int>(rel & 31);
+// One destination 32-bit word of a run, `wr` = its first bit relative to the run start
+// (the run owns bits [0, len); its first nsrc bits come from `src`, a 16-byte aligned
+// shared row, the rest up to len is zero pad): plain store when the run owns the whole
+// word, otherwise a masked atomic clear + set of the run's own bits (a neighbouring run
+// owns the rest of the word).
+__device__ __forceinline__ void put_word(uint32_t* dst, int wr, int len, int nsrc, const uint32_t* src) {
+  const int q = wr >> 5;
+  const int r = wr & 31;
+  const int nsw = (nsrc + 31) >> 5;
   const uint32_t lo = (q >= 0 && q < nsw) ? src[q] : 0u;
   const uint32_t hi = (q + 1 >= 0 && q + 1 < nsw) ? src[q + 1] : 0u;
-  uint32_t v = __funnelshift_r(lo, hi, r);
-  const int vlo = static_cast<int>(min64(max64(-rel, 0), 32));
-  const int vhi = static_cast<int>(min64(max64(nsrc - rel, 0), 32));
-  v &= bit_range_mask(vlo, vhi);
-  const int olo = static_cast<int>(min64(max64(B - W * 32, 0), 32));
-  const int ohi = static_cast<int>(min64(max64(E - W * 32, 0), 32));
-  const uint32_t own = bit_range_mask(olo, ohi);
+  const int first = max(-wr, 0);
+  const uint32_t v = __funnelshift_r(lo, hi, r) & bit_range_mask(first, min(max(nsrc - wr, 0), 32));
+  const uint32_t own = bit_range_mask(first, min(max(len - wr, 0), 32));
   if (own == 0xFFFFFFFFu) {
-    dst32[W] = v;
+    *dst = v;
   } else if (own != 0u) {
-    atomicAnd(dst32 + W, ~own);
-    atomicOr(dst32 + W, v & own);
+    atomicAnd(dst, ~own);
+    atomicOr(dst, v & own);
   }
 }
 
@@ -558,35 +568,36 @@ __global__ void __launch_bounds__(kThreads) pack_tiles(const TileArgs args) {
     for (int i = tid; i < cnt; i += kThreads) {
       const int c = i / Vmax;
       const int v = i - c * Vmax;
-      const int64_t B = pm[c].a;
-      if (B < 0) continue;
-      const int64_t E = B + pm[c].b;
-      const int64_t V = (B >> 7) + v;
-      if (V > ((E - 1) >> 7)) continue;
-      const int64_t nsrc = static_cast<int64_t>(tc.n) * pm[c].c;
+      const RowMeta m = pm[c];
+      if (m.a < 0) continue;
+      const int len = m.b;                                     // run bits incl. pad
+      const int rel = (v << 7) - static_cast<int>(m.a & 127);  // vector's first bit, run-relative
+      if (rel >= len) continue;
+      const int nsrc = tc.n * m.c;
+      const int64_t V = (m.a >> 7) + v;
       const uint32_t* src = reinterpret_cast<const uint32_t*>(pbase + c * rs);
-      const int64_t rel = V * 128 - B;  // source bit of the vector's first bit
-      if (rel >= 0 && rel + 128 <= nsrc && V * 128 + 128 <= E) {
-        // fully owned vector made of source bits only: whole 16-byte store, the run's
-        // bit offset applied with funnel shifts (src[q + 4] < nsrc when r > 0)
-        const int q = static_cast<int>(rel >> 5);
-        const int r = static_cast<int>(rel & 31);
+      if (rel >= 0 && rel + 128 <= nsrc && rel + 128 <= len) {
+        // fully owned vector made of source bits only: whole 16-byte store, the run's bit
+        // offset applied with funnel shifts (src[q + 4] holds source bits when r > 0)
+        const int q = rel >> 5;
+        const int r = rel & 31;
         uint4 w;
         if (r == 0) {
           if ((q & 3) == 0) w = *reinterpret_cast<const uint4*>(src + q);
           else w = make_uint4(src[q], src[q + 1], src[q + 2], src[q + 3]);
         } else {
-          const uint32_t s0 = src[q], s1 = src[q + 1], s2 = src[q + 2], s3 = src[q + 3], s4 = src[q + 4];
-          w = make_uint4(__funnelshift_r(s0, s1, r), __funnelshift_r(s1, s2, r), __funnelshift_r(s2, s3, r),
-                         __funnelshift_r(s3, s4, r));
+          uint32_t sw[5];
+          words5(src, q, sw);
+          w = make_uint4(__funnelshift_r(sw[0], sw[1], r), __funnelshift_r(sw[1], sw[2], r),
+                         __funnelshift_r(sw[2], sw[3], r), __funnelshift_r(sw[3], sw[4], r));
         }
         st_global_cs16(dst32 + 4 * V, w);
       } else {
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          const int64_t W = 4 * V + k;
-          if (W * 32 + 32 <= B || W * 32 >= E) continue;
-          put_word(dst32, W, B, E, nsrc, src);
+          const int wr = rel + 32 * k;
+          if (wr + 32 <= 0 || wr >= len) continue;
+          put_word(dst32 + 4 * V + k, wr, len, nsrc, src);
         }
       }
     }

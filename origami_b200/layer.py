@@ -221,16 +221,18 @@ def scatter_blocks(value: torch.Tensor, kv_layer: torch.Tensor, block_ids, *,
 
 
 def fused_kernel_name(fmt: LayerFormat, restore: bool = True) -> str:
-    """Name of the kernel the fused op launches for this format: the persistent TMA
-    kernels for aligned preset formats, the generic tile kernels otherwise (the rule of
-    tma_eligible in csrc/abi.cu; the packed buffer is assumed 16-byte aligned)."""
+    """Name of the kernel the fused op launches for this format (the dispatch rules of
+    csrc/abi.cu: TMA tensor-map kernels for 16-byte aligned runs, bulk-copy kernels for
+    byte-aligned contiguous runs, generic tile kernels otherwise; the packed buffer is
+    assumed 16-byte aligned)."""
     presets = {(8, 0): (8, 8), (7, 15, 0): (8, 1, 7), (10, 8, 0): (6, 2, 8)}
     D, T = fmt.head_dim, fmt.num_tokens
     tt = 8 * (2048 // D)
-    aligned = (presets.get(tuple(fmt.planes.shifts)) == tuple(fmt.planes.bits) and D in (64, 128, 256)
-               and all((T * b) % 128 == 0 and (tt * b) % 128 == 0 for b in fmt.planes.bits))
-    if aligned:
+    preset = presets.get(tuple(fmt.planes.shifts)) == tuple(fmt.planes.bits) and D in (64, 128, 256)
+    if preset and all((T * b) % 128 == 0 and (tt * b) % 128 == 0 for b in fmt.planes.bits):
         return "restore_tma" if restore else "pack_tma"
+    if preset and all((T * b) % 8 == 0 for b in fmt.planes.bits):
+        return "restore_bulk" if restore else "pack_bulk"
     return "restore_tiles" if restore else "pack_tiles"
 
 

@@ -22,6 +22,10 @@ GEOMS = [
     (1040, 16, 2, 128, 1 << 20),  # aligned runs, partial last tile (TMA path for byte planes)
     (2048, 32, 4, 64, 1 << 20),
     (512, 16, 2, 256, 1 << 20),
+    # ragged runs over many tiles per persistent CTA: vectors carried between tiles
+    (20000, 16, 8, 128, 1 << 20),
+    (30000, 32, 4, 64, 1 << 18),
+    (12345, 16, 4, 256, 1 << 20),
 ]
 PLANES = [BYTE_PLANES, BF16_BIT_PLANES, FP16_BIT_PLANES, ODD_PLANES]
 
@@ -141,7 +145,7 @@ def test_raw_gather_scatter_match_torch(cuda, kv_first):
 
 
 @pytest.mark.parametrize("planes", [BYTE_PLANES, BF16_BIT_PLANES, FP16_BIT_PLANES, ODD_PLANES], ids=lambda p: p.name)
-@pytest.mark.parametrize("T, jobs", [(1024, 5), (1000, 3), (256, 131)])
+@pytest.mark.parametrize("T, jobs", [(1024, 5), (1000, 3), (256, 131), (3000, 40)])
 def test_batched_jobs_match_per_job(oracle, cuda, planes, T, jobs):
     """Batched pack/restore over several layers (own caches, own block tables) gives the
     per-job results and the oracle's bytes; 131 jobs span two persistent launches."""
