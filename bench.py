@@ -46,7 +46,8 @@ def parse_args():
     ap.add_argument("--impl", choices=("origami", "reference"), default="origami")
     ap.add_argument("--planes", default="byte", help="byte | bit | bf16_bits | fp16_bits")
     ap.add_argument("--layers", type=int, default=0, help="layers (default: 32 for C2, 4 for C3, 8 for C5)")
-    ap.add_argument("--config", choices=("C2", "C3", "C5"), default="C2", help="workload (C2 is the headline)")
+    ap.add_argument("--config", choices=("C2", "C3", "C5", "CG", "KIVI"), default="C2",
+                    help="workload (C2 is the headline; CG / KIVI: quantized restore paths)")
     ap.add_argument("--chunk-bytes", type=int, default=1 << 20, help="codec chunk size (min = target = max)")
     ap.add_argument("--tokens", type=int, default=0, help="C2 only: tokens per request (default 32768)")
     ap.add_argument("--no-e2e", action="store_true")
@@ -96,6 +97,16 @@ def max_over_ranks(x: float, world: int, device=None) -> float:
     t = torch.tensor([x], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def any_over_ranks(flag: bool, world: int, device=None) -> bool:
+    return max_over_ranks(1.0 if flag else 0.0, world, device) > 0.5
+
+
+# A sleep kernel of this many cycles (about 50 ms at the B200's 1965 MHz) runs ahead of
+# every timed pass, so that the host has enqueued the pass before the GPU reaches it.
+HEAD_START_CYCLES = int(1e8)
+HEAD_START_S = 0.04
 
 
 # ----------------------------------------------------------------------------------------
@@ -339,33 +350,46 @@ def run_origami(args, rank, world, local):
 
     def timed(step_fn):
         """Per-launch CUDA-event durations from an eager pass, then the step time from
-        CUDA-graph replays of the same step (no host launch overhead in `value`)."""
+        CUDA-graph replays of the same step (no host launch overhead in `value`).
+
+        Both passes start behind a sleep kernel, so the GPU is still busy while the host
+        enqueues and the events bracket device work only; a pass whose host enqueue
+        outlasted that head start (a stalled host thread, e.g. while nvidia-smi polls the
+        driver) is measured again."""
         for _ in range(args.warmup):
             step_fn()
         torch.cuda.synchronize(device)
-        # per-launch durations: a sleep kernel gives the GPU a head start so every event
-        # pair brackets a kernel, not host-side argument preparation
-        launch_events = []
-        torch.cuda._sleep(int(2e7))
-        t_host = time.perf_counter()
-        step_fn(launch_events)
-        host_us = (time.perf_counter() - t_host) * 1e6 / max(1, len(launch_events))
-        torch.cuda.synchronize(device)
+        for _attempt in range(4):
+            launch_events = []
+            torch.cuda._sleep(HEAD_START_CYCLES)
+            t_host = time.perf_counter()
+            step_fn(launch_events)
+            host_s = time.perf_counter() - t_host
+            torch.cuda.synchronize(device)
+            if host_s < HEAD_START_S:
+                break
         launch_ms_sum = sum(a.elapsed_time(b) for a, b in launch_events)
-        host_us_per_call.append(host_us)
+        host_us_per_call.append(host_s * 1e6 / max(1, len(launch_events)))
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
             step_fn()
         for _ in range(args.warmup):
             graph.replay()
-        barrier(world)
-        torch.cuda.synchronize(device)
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        t0.record(stream)
-        for _ in range(args.steps):
-            graph.replay()
-        t1.record(stream)
-        torch.cuda.synchronize(device)
+        for _attempt in range(4):
+            barrier(world)
+            torch.cuda.synchronize(device)
+            torch.cuda._sleep(HEAD_START_CYCLES)
+            t_host = time.perf_counter()
+            t0.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            t1.record(stream)
+            host_s = time.perf_counter() - t_host
+            torch.cuda.synchronize(device)
+            # every rank takes the same number of attempts
+            if not any_over_ranks(host_s >= HEAD_START_S, world, device):
+                break
         barrier(world)
         ms = t0.elapsed_time(t1)
         del graph
@@ -788,9 +812,324 @@ def run_reference(args, rank, world):
     return 0
 
 
+# ----------------------------------------------------------------------------------------
+# quantized restore paths: CacheGen / KIVI dequantize-to-cache (--config CG | KIVI)
+# ----------------------------------------------------------------------------------------
+QUANT = {
+    # Llama-3-8B-shaped request of C2 (32 layers, 8 KV heads, head_dim 128, 32768 tokens,
+    # block 16, bf16 cache); CacheGen bins of the reference's quant level 2 fallback
+    # (cachegen_adapter.py:49-57: key 32 / value 16 bins -> 5 / 4 bits, fp16 per-token max);
+    # KIVI defaults of kivi_adapter.py:138-145 (2 bits, group 64, 128 sink tokens, fp16
+    # scale / zero / sink).
+    "CG": dict(layers=32, T=32768, H=8, D=128, bs=16, key_bins=32, value_bins=16),
+    "KIVI": dict(layers=32, T=32768, H=8, D=128, bs=16, bits=2, group_size=64, sink=128),
+}
+
+
+class QuantWorkload:
+    """Per-layer quantized payloads (seeded random streams and metadata, the same bytes
+    for both arms) and a paged bf16 cache per layer, all resident on the device."""
+
+    def __init__(self, kind: str, layers: int, device, seed: int = 7):
+        import torch
+
+        q = QUANT[kind]
+        self.kind, self.q = kind, q
+        self.layers = layers
+        T, H, D, bs = q["T"], q["H"], q["D"], q["bs"]
+        C = H * D
+        self.T, self.H, self.D, self.bs, self.C = T, H, D, bs, C
+        nb = (T + bs - 1) // bs
+        self.NB = nb + 64
+        g = torch.Generator(device="cpu").manual_seed(seed)
+        self.ids = torch.randperm(self.NB, generator=g)[:nb].to(device)
+        gd = torch.Generator(device=device).manual_seed(seed)
+
+        def rbytes(n):
+            return torch.randint(0, 256, (n,), generator=gd, dtype=torch.uint8, device=device)
+
+        # One blob per layer, as the adapters lay out their raw payload (the symbol streams
+        # followed by the fp16 metadata, cachegen_adapter.py:288-300, kivi_adapter.py:361-392);
+        # the ops read typed views of it.
+        parts: list[tuple[str, int, str]] = []  # name, bytes, dtype
+        if kind == "CG":
+            kb = (q["key_bins"] - 1).bit_length()
+            vb = (q["value_bins"] - 1).bit_length()
+            self.key_bits, self.value_bits = kb, vb
+            self.klen, self.vlen = (T * C * kb + 7) // 8, (T * C * vb + 7) // 8
+            parts = [("key", self.klen, "u8"), ("value", self.vlen, "u8"), ("max_key", 2 * T, "f16"),
+                     ("max_value", 2 * T, "f16")]
+        else:
+            b, gs, sink = q["bits"], q["group_size"], q["sink"]
+            body = T - sink
+            slen = (body * C * b + 7) // 8
+            kg, vg = (body + gs - 1) // gs, (C + gs - 1) // gs
+            self.klen = self.vlen = slen
+            parts = [("key", slen, "u8"), ("value", slen, "u8"), ("key_scale", 2 * kg * C, "f16"),
+                     ("key_zero", 2 * kg * C, "f16"), ("value_scale", 2 * body * vg, "f16"),
+                     ("value_zero", 2 * body * vg, "f16"), ("key_sink", 2 * sink * C, "f16"),
+                     ("value_sink", 2 * sink * C, "f16")]
+        self.offsets, off = {}, 0
+        for name, n, _ in parts:
+            off = (off + 15) // 16 * 16
+            self.offsets[name] = (off, n)
+            off += n
+        self.blob_bytes = off
+        self.in_bytes = sum(n for _, n, _ in parts)
+        ranges = {"max_key": (0.0, 1.0), "max_value": (0.0, 1.0), "key_scale": (0.001, 0.5),
+                  "value_scale": (0.001, 0.5), "key_zero": (-2, 2), "value_zero": (-2, 2), "key_sink": (-8, 8),
+                  "value_sink": (-8, 8)}
+        self.blobs = []
+        for _ in range(layers):
+            blob = torch.zeros(self.blob_bytes, dtype=torch.uint8, device=device)
+            for name, n, dt in parts:
+                o = self.offsets[name][0]
+                if dt == "u8":
+                    blob[o:o + n] = rbytes(n)
+                elif name.startswith("max"):
+                    blob[o:o + n].view(torch.float16)[:] = torch.exp(
+                        torch.randn(n // 2, generator=gd, device=device)).half()
+                else:
+                    lo, hi = ranges[name]
+                    blob[o:o + n].view(torch.float16)[:] = (
+                        torch.rand(n // 2, generator=gd, device=device) * (hi - lo) + lo).half()
+            self.blobs.append(blob)
+        self.kv_bytes = 2 * T * C * 2
+        self.caches = [torch.zeros((2, self.NB, bs, H, D), dtype=torch.bfloat16, device=device)
+                       for _ in range(layers)]
+
+    def view(self, blob, name):
+        import torch
+
+        o, n = self.offsets[name]
+        return blob[o:o + n].view(torch.float16)
+
+    def call(self, fn_cg, fn_kivi, layer: int, blob=None, error_count=None):
+        """One layer's fused restore from `blob` (default: the layer's resident blob)."""
+        q = self.q
+        blob = self.blobs[layer] if blob is None else blob
+        kw = {} if error_count is None else {"error_count": error_count}
+        ko, vo = self.offsets["key"][0], self.offsets["value"][0]
+        if self.kind == "CG":
+            fn_cg(blob, ko, self.klen, vo, self.vlen, self.key_bits, self.value_bits, q["key_bins"],
+                  q["value_bins"], self.view(blob, "max_key"), self.view(blob, "max_value"), self.caches[layer],
+                  self.ids, self.T, self.H, self.D, **kw)
+        else:
+            fn_kivi(blob, ko, self.klen, vo, self.vlen, q["bits"], q["group_size"], q["sink"],
+                    self.view(blob, "key_scale"), self.view(blob, "key_zero"), self.view(blob, "value_scale"),
+                    self.view(blob, "value_zero"), self.view(blob, "key_sink"), self.view(blob, "value_sink"),
+                    self.caches[layer], self.ids, self.T, self.H, self.D, **kw)
+
+    def oracle_layer(self, layer: int) -> np.ndarray:
+        """The CPU oracle's cache for one layer (checker; also the timed CPU sample)."""
+        sys.path.insert(0, str(REPO / "oracle"))
+        import oracle
+
+        q = self.q
+        cache = np.zeros((2, self.NB, self.bs, self.H, self.D), dtype=np.uint16)
+        blob = self.blobs[layer].cpu().numpy()
+        ids = self.ids.cpu().numpy()
+        ko, vo = self.offsets["key"][0], self.offsets["value"][0]
+
+        def h(name):
+            o, n = self.offsets[name]
+            return blob[o:o + n].view(np.float16)
+
+        if self.kind == "CG":
+            oracle.cachegen_to_cache(blob, ko, self.klen, vo, self.vlen, self.key_bits, self.value_bits,
+                                     q["key_bins"], q["value_bins"], h("max_key"), h("max_value"), cache, False, ids,
+                                     self.T, True)
+        else:
+            oracle.kivi_to_cache(blob, ko, self.klen, vo, self.vlen, q["bits"], q["group_size"], q["sink"],
+                                 h("key_scale"), h("key_zero"), h("value_scale"), h("value_zero"), h("key_sink"),
+                                 h("value_sink"), cache, False, ids, self.T, True)
+        return cache
+
+
+def _graph_timed(step_fn, args, world, device):
+    """Warm-up, per-launch CUDA events (eager, behind a sleep head start), then CUDA-graph
+    replays of the step; the same method as the C2 line."""
+    import torch
+
+    stream = torch.cuda.current_stream(device)
+    for _ in range(args.warmup):
+        step_fn()
+    torch.cuda.synchronize(device)
+    for _attempt in range(4):
+        ev = []
+        torch.cuda._sleep(HEAD_START_CYCLES)
+        t_host = time.perf_counter()
+        step_fn(ev)
+        host_s = time.perf_counter() - t_host
+        torch.cuda.synchronize(device)
+        if host_s < HEAD_START_S:
+            break
+    launch_ms = [a.elapsed_time(b) for a, b in ev]
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step_fn()
+    for _ in range(args.warmup):
+        graph.replay()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for _attempt in range(4):
+        barrier(world)
+        torch.cuda.synchronize(device)
+        torch.cuda._sleep(HEAD_START_CYCLES)
+        t_host = time.perf_counter()
+        t0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        t1.record(stream)
+        host_s = time.perf_counter() - t_host
+        torch.cuda.synchronize(device)
+        if not any_over_ranks(host_s >= HEAD_START_S, world, device):
+            break
+    barrier(world)
+    ms = max_over_ranks(t0.elapsed_time(t1), world, device)
+    del graph
+    return ms, launch_ms
+
+
+def run_quant(args, rank, world, local, impl: str):
+    """--config CG | KIVI: the fused dequantize-to-cache restore of one request's layers.
+    `impl` origami times liborigami_b200.so; reference times the reference's own CUDA
+    kernels (csrc/origami/bitpack_layout_cuda.cu:348-423, 577-683) built from its sources
+    into oracle/_ref (rank 0 only)."""
+    import torch
+
+    kind = args.config
+    metric = {"CG": "KV restore GB/s (CacheGen unpack + dequantize + paged scatter), whole job",
+              "KIVI": "KV restore GB/s (KIVI unpack + dequantize + paged scatter), whole job"}[kind]
+    if impl == "reference":
+        if rank != 0:
+            return 0
+        sys.path.insert(0, str(REPO / "tests" / "golden"))
+        from make_ref_vectors import load_reference_extension
+
+        ext = load_reference_extension()
+        if ext is None:
+            print(json.dumps({"impl": "reference", "unavailable": "reference extension not built in oracle/_ref "
+                              "(python oracle/build_ref.py needs the reference sources)"}), flush=True)
+            return 0
+        fn_cg, fn_kivi = ext.cachegen_unpack_dequantize_to_kv_cache_cuda, ext.kivi_dequantize_to_kv_cache_cuda
+        world_eff = 1
+    else:
+        from origami_b200 import quant
+
+        fn_cg, fn_kivi = quant.cachegen_unpack_dequantize_to_kv_cache_cuda, quant.kivi_dequantize_to_kv_cache_cuda
+        world_eff = world
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    layers = args.layers or QUANT[kind]["layers"]
+    wl = QuantWorkload(kind, layers, device, seed=7 + rank)
+    err = torch.zeros(1, dtype=torch.int32, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    def step(events=None):
+        for layer in range(layers):
+            if events is not None:
+                events.append((torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)))
+                events[-1][0].record(stream)
+            if impl == "reference":
+                wl.call(fn_cg, fn_kivi, layer)
+            else:
+                wl.call(fn_cg, fn_kivi, layer, error_count=err)
+            if events is not None:
+                events[-1][1].record(stream)
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    ms, launch_ms = _graph_timed(step, args, world_eff, device)
+    clock_info = clocks.stop()
+    steps = args.steps
+    kv_gbs = wl.kv_bytes * layers * world_eff * steps / (ms / 1e3) / GB
+    alg = wl.kv_bytes + wl.in_bytes
+    peak, peak_kind = measured_hbm_peak()
+    mean_launch = sum(launch_ms) / len(launch_ms)
+    kernel = {"CG": "cachegen_to_cache", "KIVI": "kivi_to_cache"}[kind]
+    if impl == "reference":
+        kernel = {"CG": "cachegen_unpack_dequantize_to_kv_cache_kernel",
+                  "KIVI": "kivi_dequantize_to_kv_cache_kernel"}[kind]
+    roof = {"kernel": kernel, "bound": "hbm", "achieved": round(alg / (mean_launch / 1e3) / GB, 1), "peak": peak,
+            "peak_kind": peak_kind, "unit": "GB/s", "frac": round(alg / (mean_launch / 1e3) / GB / peak, 4),
+            "traffic": None, "algorithmic_bytes_per_launch": alg, "launch_ms": round(mean_launch, 5)}
+    q = QUANT[kind]
+    cfgd = {"workload": f"{kind}: Llama-3-8B-shaped request, {q['T']} tokens, {q['H']} KV heads per rank, "
+                        f"head_dim {q['D']}, block {q['bs']}, bf16 paged cache, seeded permuted block table",
+            "layers": layers, "requests": world_eff, **{k: v for k, v in q.items() if k != "layers"},
+            "parallelism": f"kv-head shard x{world_eff}, no collective",
+            "l2": f"inputs larger than L2 ({layers * (wl.kv_bytes + wl.in_bytes) / 2**30:.1f} GiB per rank per step)"}
+
+    # verification and CPU sample: layer 0 against the oracle
+    ok = True
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        t0 = time.perf_counter()
+        want = wl.oracle_layer(0)
+        dt = time.perf_counter() - t0
+        got = wl.caches[0].view(torch.int16).cpu().numpy().view(np.uint16)
+        ok = bool(np.array_equal(got, want))
+        cpu = {"value": round(wl.kv_bytes / dt / GB, 3), "unit": "GB/s", "cores": 1, "kind": "port",
+               "sample": f"1 layer ({wl.kv_bytes / 2**20:.0f} MiB KV), oracle {kind} restatement, {dt:.1f} s"}
+    if impl == "origami":
+        ok = ok and int(err.item()) == 0
+
+    e2e = None
+    if impl == "origami" and not args.no_e2e:
+        host = [b.cpu().pin_memory() for b in wl.blobs]
+        dev = torch.empty_like(wl.blobs[0])
+        err_h = torch.zeros(1, dtype=torch.int32).pin_memory()
+
+        def e2e_step():
+            for layer in range(layers):
+                dev.copy_(host[layer], non_blocking=True)
+                wl.call(fn_cg, fn_kivi, layer, blob=dev, error_count=err)
+            err_h.copy_(err, non_blocking=True)
+
+        for _ in range(args.warmup):
+            e2e_step()
+        torch.cuda.synchronize(device)
+        barrier(world)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(steps):
+            e2e_step()
+        b.record(stream)
+        torch.cuda.synchronize(device)
+        ms_e2e = max_over_ranks(a.elapsed_time(b), world, device)
+        h2d = sum(int(h.numel()) for h in host)
+        e2e = {"value": round(wl.kv_bytes * layers * world * steps / (ms_e2e / 1e3) / GB, 1), "unit": "GB/s",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4, "ms_per_step": round(ms_e2e / steps, 3),
+               "note": "each layer's payload blob (streams + metadata) copied from pinned host, then the fused "
+                       "restore"}
+
+    if rank == 0:
+        line = {"metric": metric, "value": round(kv_gbs, 1), "unit": "GB/s", "n_gpus": world_eff, "steps": steps,
+                "warmup": args.warmup, "ms_per_step": round(ms / steps, 4), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "bf16 out (fp32 dequant math)",
+                "data": "synthetic (seeded random symbol streams and metadata)", "config": cfgd, "roofline": roof,
+                "gpu_launches": layers if impl == "origami" else 0, "clocks": clock_info, "verified": ok}
+        if impl == "reference":
+            line["impl"] = "reference"
+            line["cpu_baseline"] = {"value": round(kv_gbs, 1), "unit": "GB/s", "cores": 0, "kind": "reference",
+                                    "sample": "the reference's CUDA kernel on the GPU (no CPU implementation exists)"}
+            line["e2e"] = {"value": round(kv_gbs, 1), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+        else:
+            if cpu is not None:
+                line["cpu_baseline"] = cpu
+            if e2e is not None:
+                line["e2e"] = e2e
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+
 def main():
     args = parse_args()
-    if args.impl == "reference":
+    if args.config in QUANT:
+        rank, world, local = init_dist("nccl")
+        rc = run_quant(args, rank, world, local, args.impl)
+    elif args.impl == "reference":
         rank, world, _ = init_dist("gloo")
         rc = run_reference(args, rank, world)
     else:

@@ -206,6 +206,63 @@ int32_t origami_scatter_blocks(const void* d_in, int64_t in_bytes,
                                const int64_t* d_block_ids, int64_t num_block_ids,
                                uint32_t* d_error_count, origami_stream_t stream);
 
+/* ---------------------------------------------------------------------------------
+ * Quantized (lossy) restore paths: fused dequantize into the paged cache
+ * ------------------------------------------------------------------------------- */
+
+/* Element types of the tensors below. */
+enum {
+  ORIGAMI_DTYPE_F16 = 1,
+  ORIGAMI_DTYPE_BF16 = 2,
+  ORIGAMI_DTYPE_F32 = 3
+};
+
+/* Drop-in for cachegen_unpack_dequantize_to_kv_cache_cuda (bitpack_layout_cuda.cpp:475-580,
+ * kernel bitpack_layout_cuda.cu:348-423; called by quantization/cachegen_adapter.py:770).
+ * Key / value symbol streams (token > head > head_dim order, dense LSB-first, bits 1..8)
+ * live at d_bytestream + key_offset / value_offset; each element becomes
+ * ((s - c) / c) * max[token] with c = bins / 2 - 1, written as cache_dtype (F16 or BF16)
+ * into cache rows d_block_ids[token / block_size]. max_dtype is F16 or F32 (both tensors).
+ * Same checks and messages as the reference; out-of-range block ids are skipped and, when
+ * d_error_count is given, counted once per (kv, token, head) row. */
+int32_t origami_cachegen_unpack_dequantize_to_kv_cache(
+    const uint8_t* d_bytestream, int64_t bytestream_bytes, int64_t key_offset, int64_t key_bytes,
+    int64_t value_offset, int64_t value_bytes, int64_t key_bits, int64_t value_bits, int64_t key_bins,
+    int64_t value_bins, const void* d_max_key, int64_t max_key_numel, const void* d_max_value,
+    int64_t max_value_numel, int32_t max_dtype, const origami_paged_kv* cache, int32_t cache_dtype,
+    const int64_t* d_block_ids, int64_t num_block_ids, int64_t tokens, uint32_t* d_error_count,
+    origami_stream_t stream);
+
+/* Drop-in for cachegen_unpack_dequantize_cuda (bitpack_layout_cuda.cpp:402-473, kernel
+ * bitpack_layout_cuda.cu:141-185): 2 * layers streams (all key layers, then all value
+ * layers) at d_bytestream + offsets[i], bits_per_layer[i] bits each, dequantized into
+ * d_output = fp16 [layers, 2, heads, tokens, head_dim] (output_bytes bytes). Offsets and
+ * bits are given on the device (read by the kernel) and on the host (validated). */
+int32_t origami_cachegen_unpack_dequantize(
+    const uint8_t* d_bytestream, int64_t bytestream_bytes, const int64_t* d_offsets, const int64_t* h_offsets,
+    int64_t num_offsets, const int64_t* d_bits_per_layer, const int64_t* h_bits_per_layer, int64_t num_bits,
+    const int64_t* d_key_bins, int64_t num_key_bins, const int64_t* d_value_bins, int64_t num_value_bins,
+    const void* d_max_key, int64_t max_key_numel, const void* d_max_value, int64_t max_value_numel,
+    int32_t max_dtype, int64_t tokens, int64_t heads, int64_t head_dim, void* d_output, int64_t output_bytes,
+    origami_stream_t stream);
+
+/* Drop-in for kivi_dequantize_to_kv_cache_cuda (bitpack_layout_cuda.cpp:583-700, kernel
+ * bitpack_layout_cuda.cu:577-683; called by quantization/kivi_adapter.py:643). Tokens
+ * [0, sink_tokens) are copied from the sink tensors ([sink_tokens, heads * head_dim]);
+ * body token bt of channel ch = head * head_dim + dim is fma(s, scale, zero) with s at
+ * stream index (head * head_dim + dim) * body + bt (value) or (dim * heads + head) * body +
+ * bt (key), value scale/zero [body, ceil(channels / group_size)] by (bt, ch / group_size),
+ * key scale/zero [ceil(body / group_size), channels] by (bt / group_size, ch).
+ * meta_numel = element counts of {key_scale, key_zero, value_scale, value_zero, key_sink,
+ * value_sink}; meta_dtype F16 or F32 (all six). */
+int32_t origami_kivi_dequantize_to_kv_cache(
+    const uint8_t* d_bytestream, int64_t bytestream_bytes, int64_t key_offset, int64_t key_bytes,
+    int64_t value_offset, int64_t value_bytes, int64_t bits, int64_t group_size, int64_t sink_tokens,
+    const void* d_key_scale, const void* d_key_zero, const void* d_value_scale, const void* d_value_zero,
+    const void* d_key_sink, const void* d_value_sink, const int64_t* meta_numel, int32_t meta_dtype,
+    const origami_paged_kv* cache, int32_t cache_dtype, const int64_t* d_block_ids, int64_t num_block_ids,
+    int64_t tokens, uint32_t* d_error_count, origami_stream_t stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

@@ -267,3 +267,230 @@ int oracle_restore_layer(const uint8_t* packed, int P, const int32_t* shift, con
   free(chunk_bits);
   return ORACLE_OK;
 }
+
+/* ---------------------------------------------------------------------------------
+ * Quantized restore paths (CacheGen, KIVI): restatements of
+ *   cachegen_unpack_dequantize_to_kv_cache_kernel  (bitpack_layout_cuda.cu:348-423),
+ *   cachegen_unpack_dequantize_kernel               (bitpack_layout_cuda.cu:141-185),
+ *   kivi_dequantize_to_kv_cache_kernel             (bitpack_layout_cuda.cu:577-683).
+ * The float steps are the reference's, one IEEE single operation each (this file is
+ * compiled with -ffp-contract=off): CacheGen ((s - c) / c) * max, KIVI fmaf(s, scale,
+ * zero) (nvcc contracts the reference's s * scale + zero into one fused multiply-add).
+ * Pinned against the reference kernels' own outputs (tests/golden/ref_quant_vectors.npz).
+ * ------------------------------------------------------------------------------- */
+#include <math.h>
+
+static uint32_t f32_bits(float f) {
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  return u;
+}
+
+static float bits_f32(uint32_t u) {
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
+}
+
+/* IEEE-754 binary16 -> binary32 (exact). */
+float oracle_half_to_float(uint16_t h) {
+  const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+  const uint32_t exp = (h >> 10) & 0x1Fu;
+  uint32_t man = h & 0x3FFu;
+  if (exp == 0x1Fu) return bits_f32(sign | 0x7F800000u | (man << 13));
+  if (exp != 0) return bits_f32(sign | ((exp + 112u) << 23) | (man << 13));
+  if (man == 0) return bits_f32(sign);
+  /* subnormal: value = man * 2^-24 */
+  int e = -14;
+  while ((man & 0x400u) == 0) {
+    man <<= 1;
+    --e;
+  }
+  man &= 0x3FFu;
+  return bits_f32(sign | ((uint32_t)(e + 127) << 23) | (man << 13));
+}
+
+/* binary32 -> binary16, round to nearest even; NaN -> 0x7FFF (canonical). */
+uint16_t oracle_float_to_half(float f) {
+  const uint32_t u = f32_bits(f);
+  const uint32_t sign = (u >> 16) & 0x8000u;
+  const uint32_t a = u & 0x7FFFFFFFu;
+  if (a > 0x7F800000u) return 0x7FFFu;
+  if (a >= 0x477FF000u) return (uint16_t)(sign | 0x7C00u); /* >= 65520 rounds to inf */
+  if (a >= 0x38800000u) {                                     /* normal half */
+    const uint32_t r = a - 0x38000000u;                       /* rebias exponent 127 -> 15 */
+    const uint32_t q = r >> 13, rem = r & 0x1FFFu;
+    const uint32_t out = q + (rem > 0x1000u || (rem == 0x1000u && (q & 1u)));
+    return (uint16_t)(sign | out);
+  }
+  if (a < 0x33000000u) return (uint16_t)sign; /* below half the smallest subnormal */
+  {
+    /* subnormal half: value / 2^-24, rounded to nearest even */
+    const uint32_t e = a >> 23;
+    const uint32_t m = (a & 0x7FFFFFu) | 0x800000u;
+    const int shift = (int)(126 - e); /* m * 2^(e-150) / 2^-24 = m >> (126 - e), 14..24 */
+    const uint32_t q = m >> shift;
+    const uint32_t rem = m & ((1u << shift) - 1u);
+    const uint32_t half = 1u << (shift - 1);
+    const uint32_t out = q + (rem > half || (rem == half && (q & 1u)));
+    return (uint16_t)(sign | out);
+  }
+}
+
+/* binary32 -> bfloat16, round to nearest even; NaN -> 0x7FFF (canonical). */
+uint16_t oracle_float_to_bf16(float f) {
+  const uint32_t u = f32_bits(f);
+  if ((u & 0x7FFFFFFFu) > 0x7F800000u) return 0x7FFFu;
+  return (uint16_t)((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
+}
+
+static float meta_at(const void* p, int is_half, int64_t i) {
+  return is_half ? oracle_half_to_float(((const uint16_t*)p)[i]) : ((const float*)p)[i];
+}
+
+static uint16_t out_at(float v, int out_is_bf16) {
+  return out_is_bf16 ? oracle_float_to_bf16(v) : oracle_float_to_half(v);
+}
+
+/* unpack_symbol_direct (cu:295-312): dense LSB-first, bytes past src_bytes read as 0 */
+static uint8_t symbol_direct(const uint8_t* src, int64_t src_bytes, int64_t index, int bits) {
+  if (bits == 8) return index < src_bytes ? src[index] : 0;
+  const int64_t bit = index * bits, byte = bit >> 3;
+  uint32_t w = byte < src_bytes ? src[byte] : 0u;
+  if (byte + 1 < src_bytes) w |= (uint32_t)src[byte + 1] << 8;
+  return (uint8_t)((w >> (bit & 7)) & ((1u << bits) - 1u));
+}
+
+/* The reference reads 8-bit symbols unchecked (src[index], cu:74-76 and 295-297): a short
+ * 8-bit stream runs on into the rest of the bytestream. Narrower symbols stop at the
+ * stream's own length. Past the bytestream (undefined in the reference) both read 0. */
+static int64_t read_limit(int bits, int64_t stream_bytes, int64_t to_bytestream_end) {
+  return bits == 8 ? to_bytestream_end : stream_bytes;
+}
+
+static int64_t cache_index(int blocks_first, int64_t num_cache_blocks, int64_t block_size, int64_t heads,
+                           int64_t head_dim, int64_t blk, int64_t kv, int64_t offset, int64_t head, int64_t dim) {
+  if (blocks_first) return ((((blk * 2 + kv) * block_size + offset) * heads + head) * head_dim + dim);
+  return ((((kv * num_cache_blocks + blk) * block_size + offset) * heads + head) * head_dim + dim);
+}
+
+/* cu:348-423. Returns the number of (kv, token, head) rows skipped for bad block ids. */
+int64_t oracle_cachegen_to_cache(const uint8_t* bytestream, int64_t bytestream_bytes, int64_t key_offset,
+                                 int64_t key_bytes,
+                                 int64_t value_offset, int64_t value_bytes, int key_bits, int value_bits,
+                                 int64_t key_bins, int64_t value_bins, const void* max_key, const void* max_value,
+                                 int max_is_half, uint16_t* cache, int out_is_bf16, int blocks_first,
+                                 int64_t num_cache_blocks, const int64_t* block_ids, int64_t block_count,
+                                 int64_t block_size, int64_t tokens, int64_t heads, int64_t head_dim) {
+  const int64_t channels = heads * head_dim;
+  int64_t skipped = 0;
+  for (int64_t lb = 0; lb < block_count; ++lb) {
+    for (int64_t kv = 0; kv < 2; ++kv) {
+      for (int64_t off = 0; off < block_size; ++off) {
+        const int64_t token = lb * block_size + off;
+        if (token >= tokens) continue;
+        const int64_t blk = block_ids[lb];
+        if (blk < 0 || blk >= num_cache_blocks) {
+          skipped += heads;
+          continue;
+        }
+        const int is_value = kv != 0;
+        const uint8_t* stream = bytestream + (is_value ? value_offset : key_offset);
+        const int bits = is_value ? value_bits : key_bits;
+        const int64_t stream_bytes =
+            read_limit(bits, is_value ? value_bytes : key_bytes, bytestream_bytes - (is_value ? value_offset : key_offset));
+        const int64_t bins = is_value ? value_bins : key_bins;
+        const float center = (float)(bins / 2 - 1);
+        const float max_abs = meta_at(is_value ? max_value : max_key, max_is_half, token);
+        for (int64_t ch = 0; ch < channels; ++ch) {
+          const uint8_t s = symbol_direct(stream, stream_bytes, token * channels + ch, bits);
+          const float q = ((float)s - center) / center;
+          const float value = q * max_abs;
+          cache[cache_index(blocks_first, num_cache_blocks, block_size, heads, head_dim, blk, kv, off,
+                            ch / head_dim, ch % head_dim)] = out_at(value, out_is_bf16);
+        }
+      }
+    }
+  }
+  return skipped;
+}
+
+/* cu:141-185: fp16 output [layers, 2, heads, tokens, head_dim]. */
+void oracle_cachegen_unpack(const uint8_t* bytestream, int64_t bytestream_bytes, const int64_t* offsets,
+                            const int64_t* bits_per_layer,
+                            const int64_t* key_bins, const int64_t* value_bins, const void* max_key,
+                            const void* max_value, int max_is_half, uint16_t* out, int64_t layers, int64_t tokens,
+                            int64_t heads, int64_t head_dim) {
+  const int64_t channels = heads * head_dim;
+  for (int64_t sidx = 0; sidx < 2 * layers; ++sidx) {
+    const int is_value = sidx >= layers;
+    const int64_t layer = is_value ? sidx - layers : sidx;
+    const int bits = (int)bits_per_layer[sidx];
+    const int64_t base = offsets[sidx];
+    const int64_t len = read_limit(bits, offsets[sidx + 1] - base, bytestream_bytes - base);
+    const int64_t bins = is_value ? value_bins[layer] : key_bins[layer];
+    const float center = (float)(bins / 2 - 1);
+    for (int64_t t = 0; t < tokens; ++t) {
+      const float max_abs = meta_at(is_value ? max_value : max_key, max_is_half, layer * tokens + t);
+      for (int64_t ch = 0; ch < channels; ++ch) {
+        const uint8_t s = symbol_direct(bytestream + base, len, t * channels + ch, bits);
+        const float value = (((float)s - center) / center) * max_abs;
+        const int64_t h = ch / head_dim, d = ch % head_dim;
+        out[(((layer * 2 + is_value) * heads + h) * tokens + t) * head_dim + d] = oracle_float_to_half(value);
+      }
+    }
+  }
+}
+
+/* cu:577-683. Returns the number of (kv, token, head) rows skipped for bad block ids. */
+int64_t oracle_kivi_to_cache(const uint8_t* bytestream, int64_t bytestream_bytes, int64_t key_offset,
+                             int64_t key_bytes, int64_t value_offset,
+                             int64_t value_bytes, int bits, int64_t group_size, int64_t sink_tokens,
+                             const void* key_scale, const void* key_zero, const void* value_scale,
+                             const void* value_zero, const void* key_sink, const void* value_sink, int meta_is_half,
+                             uint16_t* cache, int out_is_bf16, int blocks_first, int64_t num_cache_blocks,
+                             const int64_t* block_ids, int64_t block_count, int64_t block_size, int64_t tokens,
+                             int64_t heads, int64_t head_dim) {
+  const int64_t channels = heads * head_dim;
+  const int64_t body_tokens = tokens - sink_tokens;
+  const int64_t value_groups = (channels + group_size - 1) / group_size;
+  int64_t skipped = 0;
+  for (int64_t lb = 0; lb < block_count; ++lb) {
+    for (int64_t kv = 0; kv < 2; ++kv) {
+      for (int64_t off = 0; off < block_size; ++off) {
+        const int64_t token = lb * block_size + off;
+        if (token >= tokens) continue;
+        const int64_t blk = block_ids[lb];
+        if (blk < 0 || blk >= num_cache_blocks) {
+          skipped += heads;
+          continue;
+        }
+        const int is_value = kv != 0;
+        for (int64_t ch = 0; ch < channels; ++ch) {
+          const int64_t head = ch / head_dim, dim = ch % head_dim;
+          float value;
+          if (token < sink_tokens) {
+            value = meta_at(is_value ? value_sink : key_sink, meta_is_half, token * channels + ch);
+          } else {
+            const int64_t bt = token - sink_tokens;
+            const int64_t index = is_value ? ((head * head_dim + dim) * body_tokens + bt)
+                                           : ((dim * heads + head) * body_tokens + bt);
+            const uint8_t* stream = bytestream + (is_value ? value_offset : key_offset);
+            const int64_t limit = read_limit(bits, is_value ? value_bytes : key_bytes,
+                                             bytestream_bytes - (is_value ? value_offset : key_offset));
+            const uint8_t s = symbol_direct(stream, limit, index, bits);
+            int64_t m;
+            if (is_value) m = bt * value_groups + ch / group_size;
+            else m = (bt / group_size) * channels + ch;
+            const float sc = meta_at(is_value ? value_scale : key_scale, meta_is_half, m);
+            const float ze = meta_at(is_value ? value_zero : key_zero, meta_is_half, m);
+            value = fmaf((float)s, sc, ze);
+          }
+          cache[cache_index(blocks_first, num_cache_blocks, block_size, heads, head_dim, blk, kv, off, head, dim)] =
+              out_at(value, out_is_bf16);
+        }
+      }
+    }
+  }
+  return skipped;
+}

@@ -31,7 +31,8 @@ def build() -> Path:
     """Compile oracle.c into _build/ (gcc with OpenMP)."""
     cc = shutil.which("gcc-13") or shutil.which("gcc") or "cc"
     LIB_PATH.parent.mkdir(parents=True, exist_ok=True)
-    cmd = [cc, "-O2", "-fopenmp", "-fPIC", "-std=c11", "-shared", "-o", str(LIB_PATH), str(HERE / "oracle.c")]
+    cmd = [cc, "-O2", "-fopenmp", "-fPIC", "-std=c11", "-ffp-contract=off", "-shared", "-o", str(LIB_PATH),
+           str(HERE / "oracle.c"), "-lm"]
     subprocess.run(cmd, check=True)
     return LIB_PATH
 
@@ -53,6 +54,14 @@ def lib():
                                                          ctypes.c_int64, _I64P, _U8P]
         L.oracle_restore_layer.argtypes = [_U8P, ctypes.c_int, _I32P, _I32P, _I64P, ctypes.c_int64, _I64P, _U16P] + geom + [
             _I64P, ctypes.c_int64]
+        vp, i64, i = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
+        L.oracle_cachegen_to_cache.restype = i64
+        L.oracle_cachegen_to_cache.argtypes = [vp, i64, i64, i64, i64, i64, i, i, i64, i64, vp, vp, i, vp, i, i, i64,
+                                               vp, i64, i64, i64, i64, i64]
+        L.oracle_cachegen_unpack.argtypes = [vp, i64, vp, vp, vp, vp, vp, vp, i, vp, i64, i64, i64, i64]
+        L.oracle_kivi_to_cache.restype = i64
+        L.oracle_kivi_to_cache.argtypes = [vp, i64, i64, i64, i64, i64, i, i64, i64, vp, vp, vp, vp, vp, vp, i, vp, i,
+                                           i, i64, vp, i64, i64, i64, i64, i64]
         _lib = L
     return _lib
 
@@ -238,3 +247,70 @@ def unpack_canonical_py(flat: bytes, offsets, bits, specs, shape, layout) -> np.
 
 if os.environ.get("ORIGAMI_ORACLE_THREADS"):
     set_threads(int(os.environ["ORIGAMI_ORACLE_THREADS"]))
+
+
+# ---------------------------------------------------------------------------------------
+# Quantized restore paths (restatements of bitpack_layout_cuda.cu:141-185, 348-423,
+# 577-683). Float tensors are numpy float16 / float32 arrays; caches are uint16 arrays
+# holding fp16 or bf16 bit patterns, [num_blocks, 2, bs, H, D] (blocks_first) or
+# [2, num_blocks, bs, H, D].
+# ---------------------------------------------------------------------------------------
+def _meta(a: np.ndarray) -> tuple[np.ndarray, int]:
+    a = np.ascontiguousarray(a)
+    if a.dtype == np.float16:
+        return a, 1
+    if a.dtype == np.float32:
+        return a, 0
+    raise TypeError("metadata must be float16 or float32")
+
+
+def _cache_geom(cache: np.ndarray, blocks_first: bool):
+    assert cache.dtype == np.uint16 and cache.ndim == 5 and cache.flags["C_CONTIGUOUS"]
+    nb = cache.shape[0] if blocks_first else cache.shape[1]
+    return nb, cache.shape[2], cache.shape[3], cache.shape[4]
+
+
+def cachegen_to_cache(bytestream, key_offset, key_bytes, value_offset, value_bytes, key_bits, value_bits, key_bins,
+                      value_bins, max_key, max_value, cache: np.ndarray, blocks_first: bool, block_ids, tokens: int,
+                      out_is_bf16: bool) -> int:
+    """Writes `cache` in place; returns the (kv, token, head) rows skipped for bad ids."""
+    bs_ = np.ascontiguousarray(bytestream, dtype=np.uint8)
+    mk, mh = _meta(max_key)
+    mv, mh2 = _meta(max_value)
+    assert mh == mh2
+    ids = _i64(block_ids)
+    nb, bsz, H, D = _cache_geom(cache, blocks_first)
+    return int(lib().oracle_cachegen_to_cache(
+        bs_.ctypes.data, len(bs_), key_offset, key_bytes, value_offset, value_bytes, key_bits, value_bits, key_bins, value_bins,
+        mk.ctypes.data, mv.ctypes.data, mh, cache.ctypes.data, int(out_is_bf16), int(blocks_first), nb,
+        ids.ctypes.data, len(ids), bsz, tokens, H, D))
+
+
+def cachegen_unpack(bytestream, offsets, bits, key_bins, value_bins, max_key, max_value, tokens: int, heads: int,
+                    head_dim: int) -> np.ndarray:
+    """fp16 bit patterns [layers, 2, heads, tokens, head_dim]."""
+    bs_ = np.ascontiguousarray(bytestream, dtype=np.uint8)
+    off, b, kb, vb = _i64(offsets), _i64(bits), _i64(key_bins), _i64(value_bins)
+    mk, mh = _meta(max_key)
+    mv, _ = _meta(max_value)
+    layers = len(b) // 2
+    out = np.zeros((layers, 2, heads, tokens, head_dim), dtype=np.uint16)
+    lib().oracle_cachegen_unpack(bs_.ctypes.data, len(bs_), off.ctypes.data, b.ctypes.data, kb.ctypes.data, vb.ctypes.data,
+                                 mk.ctypes.data, mv.ctypes.data, mh, out.ctypes.data, layers, tokens, heads, head_dim)
+    return out
+
+
+def kivi_to_cache(bytestream, key_offset, key_bytes, value_offset, value_bytes, bits, group_size, sink_tokens,
+                  key_scale, key_zero, value_scale, value_zero, key_sink, value_sink, cache: np.ndarray,
+                  blocks_first: bool, block_ids, tokens: int, out_is_bf16: bool) -> int:
+    """Writes `cache` in place; returns the (kv, token, head) rows skipped for bad ids."""
+    bs_ = np.ascontiguousarray(bytestream, dtype=np.uint8)
+    metas = [_meta(m) for m in (key_scale, key_zero, value_scale, value_zero, key_sink, value_sink)]
+    half = metas[0][1]
+    assert all(m[1] == half for m in metas)
+    ids = _i64(block_ids)
+    nb, bsz, H, D = _cache_geom(cache, blocks_first)
+    return int(lib().oracle_kivi_to_cache(
+        bs_.ctypes.data, len(bs_), key_offset, key_bytes, value_offset, value_bytes, bits, group_size, sink_tokens,
+        *[m[0].ctypes.data for m in metas], half, cache.ctypes.data, int(out_is_bf16), int(blocks_first), nb,
+        ids.ctypes.data, len(ids), bsz, tokens, H, D))

@@ -92,6 +92,18 @@ def _declare(L: ctypes.CDLL) -> None:
     L.origami_gather_blocks.restype = i32
     L.origami_scatter_blocks.argtypes = [_vp, i64, P(PagedKV), _vp, i64, _vp, _vp]
     L.origami_scatter_blocks.restype = i32
+    L.origami_cachegen_unpack_dequantize_to_kv_cache.argtypes = [
+        _vp, i64, i64, i64, i64, i64, i64, i64, i64, i64, _vp, i64, _vp, i64, i32, P(PagedKV), i32, _vp, i64, i64,
+        _vp, _vp]
+    L.origami_cachegen_unpack_dequantize_to_kv_cache.restype = i32
+    L.origami_cachegen_unpack_dequantize.argtypes = [
+        _vp, i64, _vp, _vp, i64, _vp, _vp, i64, _vp, i64, _vp, i64, _vp, i64, _vp, i64, i32, i64, i64, i64, _vp, i64,
+        _vp]
+    L.origami_cachegen_unpack_dequantize.restype = i32
+    L.origami_kivi_dequantize_to_kv_cache.argtypes = [
+        _vp, i64, i64, i64, i64, i64, i64, i64, i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, i32, P(PagedKV), i32, _vp,
+        i64, i64, _vp, _vp]
+    L.origami_kivi_dequantize_to_kv_cache.restype = i32
 
 
 def lib() -> ctypes.CDLL:
@@ -129,4 +141,11 @@ EXPORTS = (
     "origami_pack_layers_from_paged",
     "origami_gather_blocks",
     "origami_scatter_blocks",
+    "origami_cachegen_unpack_dequantize_to_kv_cache",
+    "origami_cachegen_unpack_dequantize",
+    "origami_kivi_dequantize_to_kv_cache",
 )
+
+ORIGAMI_DTYPE_F16 = 1
+ORIGAMI_DTYPE_BF16 = 2
+ORIGAMI_DTYPE_F32 = 3

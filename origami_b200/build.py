@@ -13,8 +13,9 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 CSRC = HERE / "csrc"
 LIB = HERE / "liborigami_b200.so"
-SOURCES = ["abi.cu"]
-DEPS = ["abi.cu", "common.cuh", "tile_kernels.cuh", "linear_kernels.cuh", "../../include/origami_b200.h"]
+SOURCES = ["abi.cu", "quant.cu"]
+# every kernel header and source, plus the public header
+DEPS = sorted(p.name for p in CSRC.iterdir() if p.suffix in (".cu", ".cuh", ".h")) + ["../../include/origami_b200.h"]
 
 NVCC_FLAGS = [
     "-O3",

@@ -16,14 +16,10 @@
 #include "tile_kernels.cuh"
 #include "tma_kernels.cuh"
 #include "bulk_kernels.cuh"
+#include "host_common.h"
 
-namespace {
+namespace origami_host {
 
-using origami::CanonStrides;
-using origami::kThreads;
-using origami::TileArgs;
-
-constexpr int32_t kVersion = 1;
 thread_local std::string g_last_error;
 
 int32_t fail(int32_t code, const char* fmt, ...) {
@@ -46,7 +42,82 @@ int32_t after_launch(const char* what) {
   return ORIGAMI_OK;
 }
 
-bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+int32_t validate_cache(const origami_paged_kv* kv, PagedGeom& g) {
+  if (kv == nullptr || kv->d_data == nullptr) return fail(ORIGAMI_ERR_INVALID, "kv cache is null");
+  if (kv->layout != ORIGAMI_KV_FIRST && kv->layout != ORIGAMI_BLOCKS_FIRST)
+    return fail(ORIGAMI_ERR_INVALID, "unknown kv cache layout %d", kv->layout);
+  if (kv->elem_bytes != 2) return fail(ORIGAMI_ERR_UNSUPPORTED, "kv cache elements must be 2 bytes (bf16/fp16)");
+  if (kv->num_blocks <= 0 || kv->block_size <= 0 || kv->num_heads <= 0 || kv->head_dim <= 0)
+    return fail(ORIGAMI_ERR_INVALID, "kv cache dimensions must be positive");
+  if (!aligned(kv->d_data, 16)) return fail(ORIGAMI_ERR_INVALID, "kv cache must be 16-byte aligned");
+  const int64_t HD = kv->num_heads * kv->head_dim;
+  const int64_t slab = kv->block_size * HD;
+  g.token_stride = HD;
+  g.head_stride = kv->head_dim;
+  if (kv->layout == ORIGAMI_KV_FIRST) {
+    g.kv_stride = kv->num_blocks * slab;
+    g.block_stride = slab;
+  } else {
+    g.kv_stride = slab;
+    g.block_stride = 2 * slab;
+  }
+  return ORIGAMI_OK;
+}
+
+// Dynamic shared memory is raised per (kernel, device) to the largest size ever launched
+// (the attribute is a maximum, so it never has to go down); resident CTAs for a
+// persistent launch (SMs x blocks per SM) are cached per (kernel, device, size).
+int32_t persistent_slots(const void* fn, int smem, int& resident) {
+  struct Attr {
+    const void* fn;
+    int dev, smem_max;
+  };
+  struct Occ {
+    const void* fn;
+    int dev, smem, slots;
+  };
+  static std::mutex mu;
+  static std::vector<Attr> attrs;
+  static std::vector<Occ> occ;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  std::lock_guard<std::mutex> lock(mu);
+  Attr* a = nullptr;
+  for (Attr& x : attrs)
+    if (x.fn == fn && x.dev == dev) a = &x;
+  if (a == nullptr || a->smem_max < smem) {
+    if ((e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess)
+      return cuda_fail(e, "cudaFuncSetAttribute");
+    if (a == nullptr) attrs.push_back({fn, dev, smem});
+    else a->smem_max = smem;
+  }
+  for (const Occ& x : occ)
+    if (x.fn == fn && x.dev == dev && x.smem == smem) {
+      resident = x.slots;
+      return ORIGAMI_OK;
+    }
+  int sms = 0, per_sm = 0;
+  if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+    return cuda_fail(e, "cudaDeviceGetAttribute");
+  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kThreads, smem)) != cudaSuccess)
+    return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+  resident = sms * std::max(per_sm, 1);
+  occ.push_back({fn, dev, smem, resident});
+  return ORIGAMI_OK;
+}
+
+}  // namespace origami_host
+
+
+namespace {
+
+using namespace origami_host;
+using origami::CanonStrides;
+using origami::TileArgs;
+
+constexpr int32_t kVersion = 1;
 
 int64_t packed_bytes_for(int64_t symbols, int64_t bits) { return (symbols * bits + 7) / 8; }
 
@@ -174,74 +245,7 @@ int32_t validate_planes(const origami_planes* pl) {
   return ORIGAMI_OK;
 }
 
-struct PagedGeom {
-  int64_t kv_stride, block_stride, token_stride, head_stride;
-};
 
-int32_t validate_cache(const origami_paged_kv* kv, PagedGeom& g) {
-  if (kv == nullptr || kv->d_data == nullptr) return fail(ORIGAMI_ERR_INVALID, "kv cache is null");
-  if (kv->layout != ORIGAMI_KV_FIRST && kv->layout != ORIGAMI_BLOCKS_FIRST)
-    return fail(ORIGAMI_ERR_INVALID, "unknown kv cache layout %d", kv->layout);
-  if (kv->elem_bytes != 2) return fail(ORIGAMI_ERR_UNSUPPORTED, "kv cache elements must be 2 bytes (bf16/fp16)");
-  if (kv->num_blocks <= 0 || kv->block_size <= 0 || kv->num_heads <= 0 || kv->head_dim <= 0)
-    return fail(ORIGAMI_ERR_INVALID, "kv cache dimensions must be positive");
-  if (!aligned(kv->d_data, 16)) return fail(ORIGAMI_ERR_INVALID, "kv cache must be 16-byte aligned");
-  const int64_t HD = kv->num_heads * kv->head_dim;
-  const int64_t slab = kv->block_size * HD;
-  g.token_stride = HD;
-  g.head_stride = kv->head_dim;
-  if (kv->layout == ORIGAMI_KV_FIRST) {
-    g.kv_stride = kv->num_blocks * slab;
-    g.block_stride = slab;
-  } else {
-    g.kv_stride = slab;
-    g.block_stride = 2 * slab;
-  }
-  return ORIGAMI_OK;
-}
-
-// Dynamic shared memory is raised per (kernel, device) to the largest size ever launched
-// (the attribute is a maximum, so it never has to go down); resident CTAs for a
-// persistent launch (SMs x blocks per SM) are cached per (kernel, device, size).
-int32_t persistent_slots(const void* fn, int smem, int& resident) {
-  struct Attr {
-    const void* fn;
-    int dev, smem_max;
-  };
-  struct Occ {
-    const void* fn;
-    int dev, smem, slots;
-  };
-  static std::mutex mu;
-  static std::vector<Attr> attrs;
-  static std::vector<Occ> occ;
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
-  std::lock_guard<std::mutex> lock(mu);
-  Attr* a = nullptr;
-  for (Attr& x : attrs)
-    if (x.fn == fn && x.dev == dev) a = &x;
-  if (a == nullptr || a->smem_max < smem) {
-    if ((e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess)
-      return cuda_fail(e, "cudaFuncSetAttribute");
-    if (a == nullptr) attrs.push_back({fn, dev, smem});
-    else a->smem_max = smem;
-  }
-  for (const Occ& x : occ)
-    if (x.fn == fn && x.dev == dev && x.smem == smem) {
-      resident = x.slots;
-      return ORIGAMI_OK;
-    }
-  int sms = 0, per_sm = 0;
-  if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
-    return cuda_fail(e, "cudaDeviceGetAttribute");
-  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kThreads, smem)) != cudaSuccess)
-    return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
-  resident = sms * std::max(per_sm, 1);
-  occ.push_back({fn, dev, smem, resident});
-  return ORIGAMI_OK;
-}
 
 template <int ELEM, int MODE, int DT>
 int32_t launch_tiles(bool restore, TileArgs& a, size_t smem, cudaStream_t st) {
@@ -738,7 +742,7 @@ extern "C" {
 
 int32_t origami_b200_version(void) { return kVersion; }
 
-const char* origami_last_error(void) { return g_last_error.c_str(); }
+const char* origami_last_error(void) { return origami_host::g_last_error.c_str(); }
 
 int64_t origami_packed_bytes(int64_t symbols, int32_t bits) { return packed_bytes_for(symbols, bits); }
 

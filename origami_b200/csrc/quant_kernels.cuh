@@ -1,0 +1,487 @@
+// Fused dequantize-to-paged-cache kernels for the reference's lossy restore paths:
+//
+//  cachegen_to_cache  <- cachegen_unpack_dequantize_to_kv_cache_kernel
+//                        (csrc/origami/bitpack_layout_cuda.cu:348-423)
+//  cachegen_unpack    <- cachegen_unpack_dequantize_kernel (bitpack_layout_cuda.cu:141-185)
+//  kivi_to_cache      <- kivi_dequantize_to_kv_cache_kernel (bitpack_layout_cuda.cu:577-683)
+//  kivi_to_cache_elem    (same op, one element per thread, for shapes the tile kernel
+//                        does not cover)
+//
+// Arithmetic is the reference's, step for step, so the results are bit-identical:
+//  CacheGen: value = ((float(s) - c) / c) * max[token], c = float(bins / 2 - 1); the
+//            quotient depends on s only, so it is tabulated once per CTA (one IEEE
+//            division per symbol value) and every element costs one multiply.
+//  KIVI:     value = fma(float(s), scale, zero) (the reference's s * scale + zero, which
+//            nvcc contracts to one fused multiply-add), sink tokens copied from the sink
+//            tensors; out-of-range block ids are skipped (and counted).
+//  Symbols are dense LSB-first at `bits` per symbol; bytes at or past a stream's length
+//  read as zero (unpack_symbol_direct, bitpack_layout_cuda.cu:295-312), except that
+//  8-bit symbols, which the reference reads unchecked, run on to the bytestream's end
+//  (the host passes that limit).
+//
+// Layout work differs from the reference: CacheGen streams are token-major, so a warp
+// decodes one (kv, token) row of the paged cache with 16-byte stores; KIVI streams are
+// channel-major (value: head > head_dim > token, key: head_dim > head > token), so a
+// CTA stages TT-token runs of every channel of one head, transposes 8x8 symbol blocks in
+// registers and writes whole cache rows.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "common.cuh"
+
+namespace origami {
+
+template <typename T>
+__device__ __forceinline__ float to_f32(T v);
+template <>
+__device__ __forceinline__ float to_f32<float>(float v) {
+  return v;
+}
+template <>
+__device__ __forceinline__ float to_f32<__half>(__half v) {
+  return __half2float(v);
+}
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) {
+  return __bfloat162float(v);
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t out_bits(float v);
+template <>
+__device__ __forceinline__ uint32_t out_bits<__half>(float v) {
+  return __half_as_ushort(__float2half_rn(v));
+}
+template <>
+__device__ __forceinline__ uint32_t out_bits<__nv_bfloat16>(float v) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(v));
+}
+
+// One symbol with the reference's bounds rule.
+__device__ __forceinline__ uint32_t symbol_at(const uint8_t* s, int64_t nbytes, int64_t index, int bits) {
+  if (bits == 8) return index < nbytes ? s[index] : 0u;
+  const int64_t bit = index * bits;
+  const int64_t byte = bit >> 3;
+  uint32_t w = byte < nbytes ? s[byte] : 0u;
+  if (byte + 1 < nbytes) w |= static_cast<uint32_t>(s[byte + 1]) << 8;
+  return (w >> (bit & 7)) & ((1u << bits) - 1u);
+}
+
+// Symbols 8k .. 8k+7 of a stream (they start on a byte boundary: byte k*bits) as eight
+// bytes (lo: symbols 0..3, hi: 4..7).
+__device__ __forceinline__ void symbols8(const uint8_t* s, int64_t nbytes, int64_t k, int bits, uint32_t& lo,
+                                         uint32_t& hi) {
+  const int64_t byte = k * bits;
+  uint64_t v;
+  if (byte + bits <= nbytes) {
+    const uintptr_t addr = reinterpret_cast<uintptr_t>(s + byte);
+    const uint64_t* p = reinterpret_cast<const uint64_t*>(addr & ~static_cast<uintptr_t>(7));
+    const int sh = static_cast<int>(addr & 7) * 8;
+    v = __ldg(p) >> sh;
+    if (sh + 8 * bits > 64) v |= __ldg(p + 1) << (64 - sh);
+  } else {
+    v = 0;
+    for (int j = 0; j < bits; ++j)
+      if (byte + j < nbytes) v |= static_cast<uint64_t>(s[byte + j]) << (8 * j);
+  }
+  spread8_rt(static_cast<uint32_t>(v), static_cast<uint32_t>(v >> 32), bits, lo, hi);
+}
+
+// ---------------------------------------------------------------------------------------
+// CacheGen -> paged cache
+// ---------------------------------------------------------------------------------------
+struct CgArgs {
+  const uint8_t* stream[2];  // key, value
+  int64_t stream_bytes[2];
+  int32_t bits[2];
+  int64_t bins[2];
+  const void* maxv[2];  // [tokens] per stream (float or half)
+  uint8_t* cache;
+  const int64_t* ids;
+  int64_t kv_stride, block_stride, token_stride;  // elements
+  int64_t num_blocks, block_size, tokens;
+  int32_t heads;
+  int32_t C;     // heads * head_dim
+  int32_t nvec;  // C / 8 (vector path) or C (scalar path)
+  uint32_t* err;
+};
+
+__device__ __forceinline__ void cg_table(float (*table)[256], const int64_t* bins) {
+  for (int i = threadIdx.x; i < 512; i += blockDim.x) {
+    const int kv = i >> 8;
+    const float center = static_cast<float>(bins[kv] / 2 - 1);
+    table[kv][i & 255] = (static_cast<float>(i & 255) - center) / center;
+  }
+  __syncthreads();
+}
+
+// A warp per (kv, token) row; VEC: eight symbols -> one 16-byte store per lane step.
+template <typename MAXT, typename OUT, bool VEC>
+__global__ void __launch_bounds__(kThreads) cachegen_to_cache(const __grid_constant__ CgArgs a) {
+  __shared__ float table[2][256];
+  cg_table(table, a.bins);
+  const int lane = threadIdx.x & 31;
+  const int64_t rows = 2 * a.tokens;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (kThreads / 32);
+  for (int64_t row = blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); row < rows; row += warps) {
+    const int kv = row >= a.tokens ? 1 : 0;
+    const int64_t t = row - kv * a.tokens;
+    const int64_t bi = t / a.block_size;
+    const int64_t blk = a.ids[bi];
+    if (blk < 0 || blk >= a.num_blocks) {  // counted per (kv, token, head) row
+      if (lane == 0 && a.err) atomicAdd(a.err, static_cast<uint32_t>(a.heads));
+      continue;
+    }
+    OUT* dst = reinterpret_cast<OUT*>(a.cache) + kv * a.kv_stride + blk * a.block_stride +
+               (t - bi * a.block_size) * a.token_stride;
+    const float m = to_f32(static_cast<const MAXT*>(a.maxv[kv])[t]);
+    const float* q = table[kv];
+    const uint8_t* s = a.stream[kv];
+    const int64_t nb = a.stream_bytes[kv];
+    const int bits = a.bits[kv];
+    if constexpr (VEC) {
+      for (int v = lane; v < a.nvec; v += 32) {
+        uint32_t lo, hi;
+        symbols8(s, nb, t * a.nvec + v, bits, lo, hi);
+        uint32_t o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t w = j < 2 ? lo : hi;
+          const int sh = (j & 1) * 16;
+          const uint32_t e0 = out_bits<OUT>(q[(w >> sh) & 0xFF] * m);
+          const uint32_t e1 = out_bits<OUT>(q[(w >> (sh + 8)) & 0xFF] * m);
+          o[j] = e0 | (e1 << 16);
+        }
+        st_global_cs16(dst + 8 * v, make_uint4(o[0], o[1], o[2], o[3]));
+      }
+    } else {
+      for (int c = lane; c < a.C; c += 32) {
+        const uint32_t sym = symbol_at(s, nb, t * a.C + c, bits);
+        reinterpret_cast<uint16_t*>(dst)[c] = static_cast<uint16_t>(out_bits<OUT>(q[sym] * m));
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// CacheGen -> [layers, 2, heads, tokens, head_dim] fp16 (no cache)
+// ---------------------------------------------------------------------------------------
+struct CgUnpackArgs {
+  const uint8_t* bytestream;
+  int64_t bytestream_bytes;
+  const int64_t* offsets;  // [2 * layers + 1], device
+  const int64_t* bits;     // [2 * layers], device
+  const int64_t* key_bins;
+  const int64_t* value_bins;
+  const void* max_key;  // [layers * tokens]
+  const void* max_value;
+  __half* out;
+  int64_t layers, tokens, heads, head_dim;
+};
+
+// grid.y = stream (kv * layers + layer); a warp per (token, head) row of that stream.
+template <typename MAXT, bool VEC>
+__global__ void __launch_bounds__(kThreads) cachegen_unpack(const __grid_constant__ CgUnpackArgs a) {
+  __shared__ float table[256];
+  const int64_t sidx = blockIdx.y;
+  const int kv = sidx >= a.layers ? 1 : 0;
+  const int64_t layer = sidx - kv * a.layers;
+  {
+    const int64_t bins = kv ? a.value_bins[layer] : a.key_bins[layer];
+    const float center = static_cast<float>(bins / 2 - 1);
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) table[i] = (static_cast<float>(i) - center) / center;
+    __syncthreads();
+  }
+  const uint8_t* s = a.bytestream + a.offsets[sidx];
+  const int bits = static_cast<int>(a.bits[sidx]);
+  // 8-bit symbols are read up to the bytestream end, as the reference's unchecked
+  // src[index] does (bitpack_layout_cuda.cu:74-76); narrower ones up to the stream length
+  const int64_t nb = bits == 8 ? a.bytestream_bytes - a.offsets[sidx] : a.offsets[sidx + 1] - a.offsets[sidx];
+  const MAXT* mx = static_cast<const MAXT*>(kv ? a.max_value : a.max_key) + layer * a.tokens;
+  const int lane = threadIdx.x & 31;
+  const int64_t C = a.heads * a.head_dim;
+  const int64_t rows = a.tokens * a.heads;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (kThreads / 32);
+  for (int64_t row = blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); row < rows; row += warps) {
+    const int64_t t = row / a.heads;
+    const int64_t h = row - t * a.heads;
+    const float m = to_f32(mx[t]);
+    __half* dst = a.out + (((layer * 2 + kv) * a.heads + h) * a.tokens + t) * a.head_dim;
+    if constexpr (VEC) {
+      const int64_t k0 = (t * C + h * a.head_dim) >> 3;
+      for (int v = lane; v < a.head_dim / 8; v += 32) {
+        uint32_t lo, hi;
+        symbols8(s, nb, k0 + v, bits, lo, hi);
+        uint32_t o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t w = j < 2 ? lo : hi;
+          const int sh = (j & 1) * 16;
+          o[j] = out_bits<__half>(table[(w >> sh) & 0xFF] * m) |
+                 (out_bits<__half>(table[(w >> (sh + 8)) & 0xFF] * m) << 16);
+        }
+        st_global_cs16(dst + 8 * v, make_uint4(o[0], o[1], o[2], o[3]));
+      }
+    } else {
+      for (int64_t d = lane; d < a.head_dim; d += 32) {
+        const uint32_t sym = symbol_at(s, nb, t * C + h * a.head_dim + d, bits);
+        reinterpret_cast<uint16_t*>(dst)[d] = static_cast<uint16_t>(out_bits<__half>(table[sym] * m));
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// KIVI -> paged cache
+// ---------------------------------------------------------------------------------------
+struct KiviArgs {
+  const uint8_t* stream[2];  // key, value
+  int64_t stream_bytes[2];
+  const void* scale[2];  // key: [key_groups, C]; value: [body_tokens, value_groups]
+  const void* zero[2];
+  const void* sink[2];  // [sink_tokens, C]
+  uint8_t* cache;
+  const int64_t* ids;
+  int64_t kv_stride, block_stride, token_stride, head_stride;  // elements
+  int64_t num_blocks, block_size, tokens, num_ids;
+  int64_t sink_tokens, body_tokens, group_size, value_groups;
+  int32_t bits, H, D;
+  int32_t tiles_per_head, num_tiles;
+  uint32_t* err;
+};
+
+// Dequantized element (kv, token t, channel ch = h * D + d) for a body token; symbol s.
+template <typename META>
+__device__ __forceinline__ float kivi_body(const KiviArgs& a, int kv, int64_t bt, int64_t ch, uint32_t s) {
+  int64_t idx;
+  if (kv) idx = bt * a.value_groups + ch / a.group_size;
+  else idx = (bt / a.group_size) * (static_cast<int64_t>(a.H) * a.D) + ch;
+  return __fmaf_rn(static_cast<float>(s), to_f32(static_cast<const META*>(a.scale[kv])[idx]),
+                   to_f32(static_cast<const META*>(a.zero[kv])[idx]));
+}
+
+template <typename META>
+__device__ __forceinline__ float kivi_sink(const KiviArgs& a, int kv, int64_t t, int64_t ch) {
+  return to_f32(static_cast<const META*>(a.sink[kv])[t * (static_cast<int64_t>(a.H) * a.D) + ch]);
+}
+
+// Stream index of (kv, head h, channel d, body token bt).
+__device__ __forceinline__ int64_t kivi_index(const KiviArgs& a, int kv, int64_t h, int64_t d, int64_t bt) {
+  const int64_t chan = kv ? h * a.D + d : d * a.H + h;
+  return chan * a.body_tokens + bt;
+}
+
+// One element per thread (any head_dim, sink count and group size).
+template <typename META, typename OUT>
+__global__ void __launch_bounds__(kThreads) kivi_to_cache_elem(const __grid_constant__ KiviArgs a) {
+  const int64_t C = static_cast<int64_t>(a.H) * a.D;
+  const int64_t total = 2 * a.tokens * C;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(kThreads) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * kThreads) {
+    const int kv = i >= a.tokens * C ? 1 : 0;
+    const int64_t r = i - kv * a.tokens * C;
+    const int64_t t = r / C;
+    const int64_t ch = r - t * C;
+    const int64_t bi = t / a.block_size;
+    const int64_t blk = a.ids[bi];
+    if (blk < 0 || blk >= a.num_blocks) {  // counted per (kv, token, head) row
+      if (ch % a.D == 0 && a.err) atomicAdd(a.err, 1u);
+      continue;
+    }
+    float v;
+    if (t < a.sink_tokens) {
+      v = kivi_sink<META>(a, kv, t, ch);
+    } else {
+      const int64_t bt = t - a.sink_tokens;
+      const int64_t h = ch / a.D;
+      const uint32_t s = symbol_at(a.stream[kv], a.stream_bytes[kv], kivi_index(a, kv, h, ch - h * a.D, bt), a.bits);
+      v = kivi_body<META>(a, kv, bt, ch, s);
+    }
+    reinterpret_cast<uint16_t*>(a.cache)[kv * a.kv_stride + blk * a.block_stride +
+                                          (t - bi * a.block_size) * a.token_stride + ch] =
+        static_cast<uint16_t>(out_bits<OUT>(v));
+  }
+}
+
+// Tile kernel: CTA = (kv, head, TT tokens) x all D channels, 256 threads as A token octets
+// x O channel octets (O = D / 8 divides 256, TT = 8 * A). Needs sink_tokens % 8 == 0 so a
+// token octet is all sink or all body. UNI (group_size % 8 == 0): the value group of a
+// channel octet and the key group of a token octet are single groups.
+template <int D>
+struct KiviGeo {
+  static constexpr int O = D / 8;
+  static constexpr int A = kThreads / O;
+  static constexpr int TT = 8 * A;
+  static constexpr int rs = TT + 16;  // staged run row: up to TT bytes (8-bit) + word slack
+  static constexpr int runs_bytes = D * rs;
+  static constexpr int rows_bytes = TT * D * 2;
+  static constexpr int smem_bytes = runs_bytes + D * 4 + TT * 8 + rows_bytes;
+};
+
+template <typename META, typename OUT, int D, bool UNI>
+__global__ void __launch_bounds__(kThreads) kivi_to_cache(const __grid_constant__ KiviArgs a) {
+  using G = KiviGeo<D>;
+  extern __shared__ __align__(16) uint8_t kivi_smem[];
+  uint8_t* runs = kivi_smem;
+  int32_t* bit0 = reinterpret_cast<int32_t*>(kivi_smem + G::runs_bytes);
+  int64_t* rowoff = reinterpret_cast<int64_t*>(kivi_smem + G::runs_bytes + D * 4);
+  uint8_t* rows_sm = kivi_smem + G::runs_bytes + D * 4 + G::TT * 8;
+  const int tid = threadIdx.x;
+  const int bits = a.bits;
+  const int64_t C = static_cast<int64_t>(a.H) * D;
+
+  for (int tile = blockIdx.x; tile < a.num_tiles; tile += gridDim.x) {
+    const int tt = tile % a.tiles_per_head;
+    const int rest = tile / a.tiles_per_head;
+    const int h = rest % a.H;
+    const int kv = rest / a.H;
+    const int64_t t0 = static_cast<int64_t>(tt) * G::TT;
+    const int64_t tb0 = max64(t0, a.sink_tokens);
+    const int64_t tb1 = min64(t0 + G::TT, a.tokens);
+    const int nbody = static_cast<int>(max64(tb1 - tb0, 0));
+
+    // row offsets through the block table
+    for (int r = tid; r < G::TT; r += kThreads) {
+      const int64_t t = t0 + r;
+      int64_t off = -1;
+      if (t < a.tokens) {
+        const int64_t bi = t / a.block_size;
+        const int64_t blk = a.ids[bi];
+        if (blk < 0 || blk >= a.num_blocks) {
+          if (a.err) atomicAdd(a.err, 1u);
+        } else {
+          off = kv * a.kv_stride + blk * a.block_stride + (t - bi * a.block_size) * a.token_stride +
+                static_cast<int64_t>(h) * a.head_stride;
+        }
+      }
+      rowoff[r] = off;
+    }
+    // stage the body run of every channel: 4-byte words from the aligned word holding its
+    // first byte; bytes at or past the stream end read as zero
+    if (nbody > 0) {
+      const uint8_t* s = a.stream[kv];
+      const uintptr_t end = reinterpret_cast<uintptr_t>(s) + static_cast<uintptr_t>(a.stream_bytes[kv]);
+      const int words = ((nbody * bits + 7) >> 3) / 4 + 2;
+      for (int i = tid; i < D * words; i += kThreads) {
+        const int d = i / words;
+        const int w = i - d * words;
+        const int64_t bitpos = kivi_index(a, kv, h, d, tb0 - a.sink_tokens) * bits;
+        const uintptr_t first = reinterpret_cast<uintptr_t>(s) + static_cast<uintptr_t>(bitpos >> 3);
+        const uintptr_t wa = (first & ~static_cast<uintptr_t>(3)) + 4u * static_cast<uintptr_t>(w);
+        uint32_t v = 0;
+        if (wa < end) {
+          v = __ldg(reinterpret_cast<const uint32_t*>(wa));
+          if (wa + 4 > end) v &= (1u << (8 * static_cast<int>(end - wa))) - 1u;
+        }
+        reinterpret_cast<uint32_t*>(runs + d * G::rs)[w] = v;
+        if (w == 0) bit0[d] = static_cast<int32_t>((first & 3u) * 8u + static_cast<uintptr_t>(bitpos & 7));
+      }
+    }
+    __syncthreads();
+
+    const int ao = tid % G::A;
+    const int o = tid / G::A;
+    const int64_t tq = t0 + 8 * ao;  // first token of this thread's octet
+    uint32_t outw[8][4];
+    if (tq < a.tokens) {
+      if (tq < a.sink_tokens) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int64_t t = min64(tq + i, a.tokens - 1);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int64_t ch = static_cast<int64_t>(h) * D + 8 * o + 2 * j;
+            outw[i][j] = out_bits<OUT>(kivi_sink<META>(a, kv, t, ch)) |
+                         (out_bits<OUT>(kivi_sink<META>(a, kv, t, ch + 1)) << 16);
+          }
+        }
+      } else {
+        // 8 tokens x 8 channels of symbols: windows per channel, 8x8 byte transpose
+        uint32_t lo[8], hi[8];
+        const int k0 = static_cast<int>(tq - tb0);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int d = 8 * o + j;
+          uint32_t v0, v1;
+          window64(runs + d * G::rs, bit0[d] + k0 * bits, v0, v1);
+          spread8_rt(v0, v1, bits, lo[j], hi[j]);
+        }
+        transpose8x8(lo, hi);  // lo[i] / hi[i]: channels 0..3 / 4..7 of token i
+        const int64_t bq = tq - a.sink_tokens;
+        const int64_t ch0 = static_cast<int64_t>(h) * D + 8 * o;
+        if constexpr (UNI) {
+          const META* sc = static_cast<const META*>(a.scale[kv]);
+          const META* ze = static_cast<const META*>(a.zero[kv]);
+          if (kv) {
+            const int64_t g = ch0 / a.group_size;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int64_t idx = min64(bq + i, a.body_tokens - 1) * a.value_groups + g;
+              const float fs = to_f32(sc[idx]);
+              const float fz = to_f32(ze[idx]);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const uint32_t w = j < 2 ? lo[i] : hi[i];
+                const int sh = (j & 1) * 16;
+                outw[i][j] = out_bits<OUT>(__fmaf_rn(static_cast<float>((w >> sh) & 0xFF), fs, fz)) |
+                             (out_bits<OUT>(__fmaf_rn(static_cast<float>((w >> (sh + 8)) & 0xFF), fs, fz)) << 16);
+              }
+            }
+          } else {
+            const int64_t base = (bq / a.group_size) * C + ch0;
+            float fs[8], fz[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              fs[j] = to_f32(sc[base + j]);
+              fz[j] = to_f32(ze[base + j]);
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const uint32_t w = j < 2 ? lo[i] : hi[i];
+                const int sh = (j & 1) * 16;
+                const int c = 2 * j;
+                outw[i][j] =
+                    out_bits<OUT>(__fmaf_rn(static_cast<float>((w >> sh) & 0xFF), fs[c], fz[c])) |
+                    (out_bits<OUT>(__fmaf_rn(static_cast<float>((w >> (sh + 8)) & 0xFF), fs[c + 1], fz[c + 1]))
+                     << 16);
+              }
+            }
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int64_t bt = min64(bq + i, a.body_tokens - 1);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint32_t w = j < 2 ? lo[i] : hi[i];
+              const int sh = (j & 1) * 16;
+              const int64_t ch = ch0 + 2 * j;
+              outw[i][j] = out_bits<OUT>(kivi_body<META>(a, kv, bt, ch, (w >> sh) & 0xFF)) |
+                           (out_bits<OUT>(kivi_body<META>(a, kv, bt, ch + 1, (w >> (sh + 8)) & 0xFF)) << 16);
+            }
+          }
+        }
+      }
+      const int phys = (o + ao) & (G::O - 1);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        *reinterpret_cast<uint4*>(rows_sm + (8 * ao + i) * (D * 2) + phys * 16) =
+            make_uint4(outw[i][0], outw[i][1], outw[i][2], outw[i][3]);
+    }
+    __syncthreads();
+    const int oc = tid % G::O;
+    for (int r = tid / G::O; r < G::TT; r += kThreads / G::O) {
+      const int64_t off = rowoff[r];
+      if (off < 0) continue;
+      st_global_cs16(reinterpret_cast<uint16_t*>(a.cache) + off + 8 * oc,
+                     *reinterpret_cast<const uint4*>(rows_sm + r * (D * 2) + ((oc + (r >> 3)) & (G::O - 1)) * 16));
+    }
+    __syncthreads();
+  }
+}
+
+}  // namespace origami

@@ -128,6 +128,24 @@ class _Extension:
                          int(head_dim), device=symbols.device)
 
 
+    # The quantized restore exports (cpp:897-901) keep the reference's positional
+    # signatures; origami_b200.quant holds the checks and the library calls.
+    def cachegen_unpack_dequantize_cuda(self, *args: Any) -> torch.Tensor:
+        from origami_b200 import quant
+
+        return quant.cachegen_unpack_dequantize_cuda(*args)
+
+    def cachegen_unpack_dequantize_to_kv_cache_cuda(self, *args: Any) -> None:
+        from origami_b200 import quant
+
+        quant.cachegen_unpack_dequantize_to_kv_cache_cuda(*args)
+
+    def kivi_dequantize_to_kv_cache_cuda(self, *args: Any) -> None:
+        from origami_b200 import quant
+
+        quant.kivi_dequantize_to_kv_cache_cuda(*args)
+
+
 _EXT = _Extension()
 
 
@@ -272,3 +290,121 @@ def pack_canonical_storage_chunks(
         torch.cuda.current_stream(target).synchronize()
         flat = host
     return [flat[int(a):int(b)] for a, b in zip(offsets[:-1], offsets[1:])]
+
+
+def cachegen_unpack_dequantize(
+    bytestream: torch.Tensor,
+    offsets: torch.Tensor,
+    bits_per_layer: torch.Tensor,
+    key_bins: torch.Tensor,
+    value_bins: torch.Tensor,
+    max_key: torch.Tensor,
+    max_value: torch.Tensor,
+    *,
+    tokens: int,
+    heads: int,
+    head_dim: int,
+) -> torch.Tensor:
+    """native_gpu.py:149-175 of the reference."""
+    ext = load_bitpack_cuda_extension()
+    dev = bytestream.device
+    return ext.cachegen_unpack_dequantize_cuda(
+        bytestream.reshape(-1).contiguous(),
+        offsets.to(device=dev, dtype=torch.int64).contiguous(),
+        bits_per_layer.to(device=dev, dtype=torch.int64).contiguous(),
+        key_bins.to(device=dev, dtype=torch.int64).contiguous(),
+        value_bins.to(device=dev, dtype=torch.int64).contiguous(),
+        max_key.contiguous(),
+        max_value.contiguous(),
+        int(tokens),
+        int(heads),
+        int(head_dim),
+    )
+
+
+def cachegen_unpack_dequantize_to_kv_cache(
+    bytestream: torch.Tensor,
+    *,
+    key_offset: int,
+    key_bytes: int,
+    value_offset: int,
+    value_bytes: int,
+    key_bits: int,
+    value_bits: int,
+    key_bins: int,
+    value_bins: int,
+    max_key: torch.Tensor,
+    max_value: torch.Tensor,
+    kv_cache: torch.Tensor,
+    block_ids: torch.Tensor,
+    tokens: int,
+    heads: int,
+    head_dim: int,
+) -> None:
+    """native_gpu.py:178-215 of the reference (called by cachegen_adapter.py:770)."""
+    ext = load_bitpack_cuda_extension()
+    ext.cachegen_unpack_dequantize_to_kv_cache_cuda(
+        bytestream.reshape(-1).contiguous(),
+        int(key_offset),
+        int(key_bytes),
+        int(value_offset),
+        int(value_bytes),
+        int(key_bits),
+        int(value_bits),
+        int(key_bins),
+        int(value_bins),
+        max_key.contiguous(),
+        max_value.contiguous(),
+        kv_cache,
+        block_ids.to(device=kv_cache.device, dtype=torch.int64).contiguous(),
+        int(tokens),
+        int(heads),
+        int(head_dim),
+    )
+
+
+def kivi_dequantize_to_kv_cache(
+    bytestream: torch.Tensor,
+    *,
+    key_offset: int,
+    key_bytes: int,
+    value_offset: int,
+    value_bytes: int,
+    bits: int,
+    group_size: int,
+    sink_tokens: int,
+    key_scale: torch.Tensor,
+    key_zero: torch.Tensor,
+    value_scale: torch.Tensor,
+    value_zero: torch.Tensor,
+    key_sink: torch.Tensor,
+    value_sink: torch.Tensor,
+    kv_cache: torch.Tensor,
+    block_ids: torch.Tensor,
+    tokens: int,
+    heads: int,
+    head_dim: int,
+) -> None:
+    """native_gpu.py:218-260 of the reference (called by kivi_adapter.py:643)."""
+    ext = load_bitpack_cuda_extension()
+    ext.kivi_dequantize_to_kv_cache_cuda(
+        bytestream.reshape(-1).contiguous(),
+        int(key_offset),
+        int(key_bytes),
+        int(value_offset),
+        int(value_bytes),
+        int(bits),
+        int(group_size),
+        int(sink_tokens),
+        key_scale.contiguous(),
+        key_zero.contiguous(),
+        value_scale.contiguous(),
+        value_zero.contiguous(),
+        key_sink.contiguous(),
+        value_sink.contiguous(),
+        kv_cache,
+        block_ids.to(device=kv_cache.device, dtype=torch.int64).contiguous(),
+        int(tokens),
+        int(heads),
+        int(head_dim),
+    )
