@@ -92,7 +92,7 @@ int32_t launch_cg_unpack(const origami::CgUnpackArgs& a, int64_t streams, cudaSt
 // ---------------------------------------------------------------------------------------
 template <typename META, typename OUT, int D, bool UNI>
 int32_t launch_kivi_tiles(origami::KiviArgs a, cudaStream_t st) {
-  using G = origami::KiviGeo<D>;
+  using G = origami::KiviGeo<D, META>;
   void (*fn)(origami::KiviArgs) = origami::kivi_to_cache<META, OUT, D, UNI>;
   a.tiles_per_head = static_cast<int32_t>((a.tokens + G::TT - 1) / G::TT);
   const int64_t tiles = 2LL * a.H * a.tiles_per_head;

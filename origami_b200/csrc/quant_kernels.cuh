@@ -69,24 +69,48 @@ __device__ __forceinline__ uint32_t symbol_at(const uint8_t* s, int64_t nbytes, 
   return (w >> (bit & 7)) & ((1u << bits) - 1u);
 }
 
-// Symbols 8k .. 8k+7 of a stream (they start on a byte boundary: byte k*bits) as eight
-// bytes (lo: symbols 0..3, hi: 4..7).
-__device__ __forceinline__ void symbols8(const uint8_t* s, int64_t nbytes, int64_t k, int bits, uint32_t& lo,
-                                         uint32_t& hi) {
+// The 64 bits holding symbols 8k .. 8k+7 of a stream (they start on a byte boundary: byte
+// k * bits), as two aligned 8-byte loads; bytes at or past nbytes read as zero.
+__device__ __forceinline__ uint64_t symbols8_raw(const uint8_t* s, int64_t nbytes, int64_t k, int bits) {
   const int64_t byte = k * bits;
-  uint64_t v;
   if (byte + bits <= nbytes) {
     const uintptr_t addr = reinterpret_cast<uintptr_t>(s + byte);
     const uint64_t* p = reinterpret_cast<const uint64_t*>(addr & ~static_cast<uintptr_t>(7));
     const int sh = static_cast<int>(addr & 7) * 8;
-    v = __ldg(p) >> sh;
+    uint64_t v = __ldg(p) >> sh;
     if (sh + 8 * bits > 64) v |= __ldg(p + 1) << (64 - sh);
-  } else {
-    v = 0;
-    for (int j = 0; j < bits; ++j)
-      if (byte + j < nbytes) v |= static_cast<uint64_t>(s[byte + j]) << (8 * j);
+    return v;
   }
+  uint64_t v = 0;
+  for (int j = 0; j < bits; ++j)
+    if (byte + j < nbytes) v |= static_cast<uint64_t>(s[byte + j]) << (8 * j);
+  return v;
+}
+
+// Symbols 8k .. 8k+7 as eight bytes (lo: symbols 0..3, hi: 4..7).
+__device__ __forceinline__ void symbols8(const uint8_t* s, int64_t nbytes, int64_t k, int bits, uint32_t& lo,
+                                         uint32_t& hi) {
+  const uint64_t v = symbols8_raw(s, nbytes, k, bits);
   spread8_rt(static_cast<uint32_t>(v), static_cast<uint32_t>(v >> 32), bits, lo, hi);
+}
+
+// Eight b-bit symbols of a 64-bit field (symbol k at bits [k*b, (k+1)*b)) -> eight
+// dequantized elements q[s] * m, packed as 16 bytes. Symbols 0..3 come from the low word,
+// 4..7 from the field shifted by 4*b; each is one shift and one mask from its table index.
+template <typename OUT>
+__device__ __forceinline__ uint4 dequant8(const float* q, float m, uint64_t field, int bits) {
+  const uint32_t mask = (1u << bits) - 1u;
+  const uint32_t w[2] = {static_cast<uint32_t>(field), static_cast<uint32_t>(field >> (4 * bits))};
+  uint32_t o[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t x = w[j >> 1];
+    const int k = 2 * (j & 1);
+    const uint32_t e0 = out_bits<OUT>(q[(x >> (k * bits)) & mask] * m);
+    const uint32_t e1 = out_bits<OUT>(q[(x >> ((k + 1) * bits)) & mask] * m);
+    o[j] = __byte_perm(e0, e1, 0x5410);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -117,9 +141,13 @@ __device__ __forceinline__ void cg_table(float (*table)[256], const int64_t* bin
   __syncthreads();
 }
 
-// A warp per (kv, token) row; VEC: eight symbols -> one 16-byte store per lane step.
+// A warp per (kv, token) row. VEC: eight symbols -> one 16-byte store; a lane first issues
+// the loads of up to kCgUnroll vectors (and the row's block id and max), then dequantizes
+// and stores them, so several loads are in flight per lane.
+constexpr int kCgUnroll = 4;
+
 template <typename MAXT, typename OUT, bool VEC>
-__global__ void __launch_bounds__(kThreads) cachegen_to_cache(const __grid_constant__ CgArgs a) {
+__global__ void __launch_bounds__(kThreads, 5) cachegen_to_cache(const __grid_constant__ CgArgs a) {
   __shared__ float table[2][256];
   cg_table(table, a.bins);
   const int lane = threadIdx.x & 31;
@@ -129,38 +157,45 @@ __global__ void __launch_bounds__(kThreads) cachegen_to_cache(const __grid_const
     const int kv = row >= a.tokens ? 1 : 0;
     const int64_t t = row - kv * a.tokens;
     const int64_t bi = t / a.block_size;
-    const int64_t blk = a.ids[bi];
-    if (blk < 0 || blk >= a.num_blocks) {  // counted per (kv, token, head) row
-      if (lane == 0 && a.err) atomicAdd(a.err, static_cast<uint32_t>(a.heads));
-      continue;
-    }
-    OUT* dst = reinterpret_cast<OUT*>(a.cache) + kv * a.kv_stride + blk * a.block_stride +
-               (t - bi * a.block_size) * a.token_stride;
-    const float m = to_f32(static_cast<const MAXT*>(a.maxv[kv])[t]);
     const float* q = table[kv];
     const uint8_t* s = a.stream[kv];
     const int64_t nb = a.stream_bytes[kv];
     const int bits = a.bits[kv];
     if constexpr (VEC) {
-      for (int v = lane; v < a.nvec; v += 32) {
-        uint32_t lo, hi;
-        symbols8(s, nb, t * a.nvec + v, bits, lo, hi);
-        uint32_t o[4];
+      for (int v0 = 0; v0 < a.nvec; v0 += 32 * kCgUnroll) {
+        uint64_t raw[kCgUnroll];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint32_t w = j < 2 ? lo : hi;
-          const int sh = (j & 1) * 16;
-          const uint32_t e0 = out_bits<OUT>(q[(w >> sh) & 0xFF] * m);
-          const uint32_t e1 = out_bits<OUT>(q[(w >> (sh + 8)) & 0xFF] * m);
-          o[j] = e0 | (e1 << 16);
+        for (int u = 0; u < kCgUnroll; ++u) {
+          const int v = v0 + lane + 32 * u;
+          raw[u] = v < a.nvec ? symbols8_raw(s, nb, t * a.nvec + v, bits) : 0;
         }
-        st_global_cs16(dst + 8 * v, make_uint4(o[0], o[1], o[2], o[3]));
+        const int64_t blk = a.ids[bi];
+        const float m = to_f32(static_cast<const MAXT*>(a.maxv[kv])[t]);
+        if (blk < 0 || blk >= a.num_blocks) break;
+        OUT* dst = reinterpret_cast<OUT*>(a.cache) + kv * a.kv_stride + blk * a.block_stride +
+                   (t - bi * a.block_size) * a.token_stride;
+#pragma unroll
+        for (int u = 0; u < kCgUnroll; ++u) {
+          const int v = v0 + lane + 32 * u;
+          if (v >= a.nvec) break;
+          st_global_cs16(dst + 8 * v, dequant8<OUT>(q, m, raw[u], bits));
+        }
       }
     } else {
-      for (int c = lane; c < a.C; c += 32) {
-        const uint32_t sym = symbol_at(s, nb, t * a.C + c, bits);
-        reinterpret_cast<uint16_t*>(dst)[c] = static_cast<uint16_t>(out_bits<OUT>(q[sym] * m));
+      const int64_t blk = a.ids[bi];
+      if (blk >= 0 && blk < a.num_blocks) {
+        OUT* dst = reinterpret_cast<OUT*>(a.cache) + kv * a.kv_stride + blk * a.block_stride +
+                   (t - bi * a.block_size) * a.token_stride;
+        const float m = to_f32(static_cast<const MAXT*>(a.maxv[kv])[t]);
+        for (int c = lane; c < a.C; c += 32) {
+          const uint32_t sym = symbol_at(s, nb, t * a.C + c, bits);
+          reinterpret_cast<uint16_t*>(dst)[c] = static_cast<uint16_t>(out_bits<OUT>(q[sym] * m));
+        }
       }
+    }
+    if (lane == 0 && a.err) {  // counted per (kv, token, head) row
+      const int64_t blk = a.ids[bi];
+      if (blk < 0 || blk >= a.num_blocks) atomicAdd(a.err, static_cast<uint32_t>(a.heads));
     }
   }
 }
@@ -212,17 +247,7 @@ __global__ void __launch_bounds__(kThreads) cachegen_unpack(const __grid_constan
     if constexpr (VEC) {
       const int64_t k0 = (t * C + h * a.head_dim) >> 3;
       for (int v = lane; v < a.head_dim / 8; v += 32) {
-        uint32_t lo, hi;
-        symbols8(s, nb, k0 + v, bits, lo, hi);
-        uint32_t o[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint32_t w = j < 2 ? lo : hi;
-          const int sh = (j & 1) * 16;
-          o[j] = out_bits<__half>(table[(w >> sh) & 0xFF] * m) |
-                 (out_bits<__half>(table[(w >> (sh + 8)) & 0xFF] * m) << 16);
-        }
-        st_global_cs16(dst + 8 * v, make_uint4(o[0], o[1], o[2], o[3]));
+        st_global_cs16(dst + 8 * v, dequant8<__half>(table, m, symbols8_raw(s, nb, k0 + v, bits), bits));
       }
     } else {
       for (int64_t d = lane; d < a.head_dim; d += 32) {
@@ -309,25 +334,36 @@ __global__ void __launch_bounds__(kThreads) kivi_to_cache_elem(const __grid_cons
 // x O channel octets (O = D / 8 divides 256, TT = 8 * A). Needs sink_tokens % 8 == 0 so a
 // token octet is all sink or all body. UNI (group_size % 8 == 0): the value group of a
 // channel octet and the key group of a token octet are single groups.
-template <int D>
+// Shared memory: [runs: D rows x rs][bit0: D x int32][rowoff: TT x int64][token rows]
+// [scale, zero: kMetaSlots x max(TT, D) META each]. The staged-run row holds up to TT
+// bytes (8-bit symbols) plus word slack; its stride is not a multiple of 128 bytes at
+// eight rows, so the two channel octets of a warp read different banks.
+constexpr int kMetaSlots = 4;
+
+template <int D, typename META>
 struct KiviGeo {
   static constexpr int O = D / 8;
   static constexpr int A = kThreads / O;
   static constexpr int TT = 8 * A;
-  static constexpr int rs = TT + 16;  // staged run row: up to TT bytes (8-bit) + word slack
+  static constexpr int rs = TT + 24;
   static constexpr int runs_bytes = D * rs;
+  static constexpr int rows_off = runs_bytes + D * 4 + TT * 8;
   static constexpr int rows_bytes = TT * D * 2;
-  static constexpr int smem_bytes = runs_bytes + D * 4 + TT * 8 + rows_bytes;
+  static constexpr int meta_off = rows_off + rows_bytes;
+  static constexpr int meta_elems = kMetaSlots * (TT > D ? TT : D);
+  static constexpr int smem_bytes = meta_off + 2 * meta_elems * static_cast<int>(sizeof(META));
 };
 
 template <typename META, typename OUT, int D, bool UNI>
 __global__ void __launch_bounds__(kThreads) kivi_to_cache(const __grid_constant__ KiviArgs a) {
-  using G = KiviGeo<D>;
+  using G = KiviGeo<D, META>;
   extern __shared__ __align__(16) uint8_t kivi_smem[];
   uint8_t* runs = kivi_smem;
   int32_t* bit0 = reinterpret_cast<int32_t*>(kivi_smem + G::runs_bytes);
   int64_t* rowoff = reinterpret_cast<int64_t*>(kivi_smem + G::runs_bytes + D * 4);
-  uint8_t* rows_sm = kivi_smem + G::runs_bytes + D * 4 + G::TT * 8;
+  uint8_t* rows_sm = kivi_smem + G::rows_off;
+  META* msc = reinterpret_cast<META*>(kivi_smem + G::meta_off);
+  META* mze = msc + G::meta_elems;
   const int tid = threadIdx.x;
   const int bits = a.bits;
   const int64_t C = static_cast<int64_t>(a.H) * D;
@@ -379,6 +415,44 @@ __global__ void __launch_bounds__(kThreads) kivi_to_cache(const __grid_constant_
         if (w == 0) bit0[d] = static_cast<int32_t>((first & 3u) * 8u + static_cast<uintptr_t>(bitpos & 7));
       }
     }
+    // UNI: this tile's scale / zero, coalesced into shared memory when they fit in
+    // kMetaSlots value groups (one token's slots per row) or key groups (one group's D
+    // channels per row); otherwise phase B reads them from global memory.
+    bool staged = false;
+    int64_t mbase = 0;  // first staged value group / key group
+    if constexpr (UNI) {
+      if (nbody > 0) {
+        const META* sc = static_cast<const META*>(a.scale[kv]);
+        const META* ze = static_cast<const META*>(a.zero[kv]);
+        if (kv) {
+          mbase = static_cast<int64_t>(h) * D / a.group_size;
+          const int ng = static_cast<int>((static_cast<int64_t>(h) * D + D - 1) / a.group_size - mbase + 1);
+          if (ng <= kMetaSlots) {
+            staged = true;
+            for (int i = tid; i < nbody * ng; i += kThreads) {
+              const int r = i / ng;
+              const int g = i - r * ng;
+              const int64_t idx = (tb0 - a.sink_tokens + r) * a.value_groups + mbase + g;
+              msc[r * kMetaSlots + g] = sc[idx];
+              mze[r * kMetaSlots + g] = ze[idx];
+            }
+          }
+        } else {
+          mbase = (tb0 - a.sink_tokens) / a.group_size;
+          const int nkg = static_cast<int>((tb1 - 1 - a.sink_tokens) / a.group_size - mbase + 1);
+          if (nkg <= kMetaSlots) {
+            staged = true;
+            for (int i = tid; i < nkg * D; i += kThreads) {
+              const int r = i / D;
+              const int d = i - r * D;
+              const int64_t idx = (mbase + r) * C + static_cast<int64_t>(h) * D + d;
+              msc[r * D + d] = sc[idx];
+              mze[r * D + d] = ze[idx];
+            }
+          }
+        }
+      }
+    }
     __syncthreads();
 
     const int ao = tid % G::A;
@@ -418,9 +492,17 @@ __global__ void __launch_bounds__(kThreads) kivi_to_cache(const __grid_constant_
             const int64_t g = ch0 / a.group_size;
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-              const int64_t idx = min64(bq + i, a.body_tokens - 1) * a.value_groups + g;
-              const float fs = to_f32(sc[idx]);
-              const float fz = to_f32(ze[idx]);
+              float fs, fz;
+              if (staged) {
+                const int r = min(k0 + i, nbody - 1);
+                const int slot = r * kMetaSlots + static_cast<int>(g - mbase);
+                fs = to_f32(msc[slot]);
+                fz = to_f32(mze[slot]);
+              } else {
+                const int64_t idx = min64(bq + i, a.body_tokens - 1) * a.value_groups + g;
+                fs = to_f32(sc[idx]);
+                fz = to_f32(ze[idx]);
+              }
 #pragma unroll
               for (int j = 0; j < 4; ++j) {
                 const uint32_t w = j < 2 ? lo[i] : hi[i];
@@ -430,12 +512,21 @@ __global__ void __launch_bounds__(kThreads) kivi_to_cache(const __grid_constant_
               }
             }
           } else {
-            const int64_t base = (bq / a.group_size) * C + ch0;
             float fs[8], fz[8];
+            if (staged) {
+              const int base = static_cast<int>(bq / a.group_size - mbase) * D + 8 * o;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              fs[j] = to_f32(sc[base + j]);
-              fz[j] = to_f32(ze[base + j]);
+              for (int j = 0; j < 8; ++j) {
+                fs[j] = to_f32(msc[base + j]);
+                fz[j] = to_f32(mze[base + j]);
+              }
+            } else {
+              const int64_t base = (bq / a.group_size) * C + ch0;
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                fs[j] = to_f32(sc[base + j]);
+                fz[j] = to_f32(ze[base + j]);
+              }
             }
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
