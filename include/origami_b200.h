@@ -22,7 +22,8 @@
  *   - plain pointers and sizes only; `d_` pointers are device memory, `h_` host;
  *   - every launch goes to the caller's stream; nothing synchronises the device;
  *   - the entry points allocate no device memory and are safe to call from
- *     several host threads at once (no shared mutable state);
+ *     several host threads at once (the only shared state, a per-kernel cache of the
+ *     shared-memory attribute and occupancy, is behind a mutex);
  *   - return ORIGAMI_OK (0) or a negative ORIGAMI_ERR_*; origami_last_error()
  *     returns a message for the calling thread's last failure;
  *   - `d_error_count` (nullable) is a device uint32 that kernels increment for
@@ -262,6 +263,48 @@ int32_t origami_kivi_dequantize_to_kv_cache(
     const void* d_key_sink, const void* d_value_sink, const int64_t* meta_numel, int32_t meta_dtype,
     const origami_paged_kv* cache, int32_t cache_dtype, const int64_t* d_block_ids, int64_t num_block_ids,
     int64_t tokens, uint32_t* d_error_count, origami_stream_t stream);
+
+/* ---------------------------------------------------------------------------------
+ * Host codec boundary (CPU only; no CUDA calls): the ORIGQZ1 chunk bundle and raw-deflate
+ * chunk coding between caller-owned host buffers (pinned staging on the restore path)
+ * ------------------------------------------------------------------------------- */
+
+/* One chunk of an ORIGQZ1 bundle: lengths from its record, the byte offset of its
+ * compressed data in the bundle and of its decoded bytes in the bundle's raw output. */
+typedef struct origami_dz_record {
+  uint32_t raw_len;
+  uint32_t comp_len;
+  int64_t comp_offset;
+  int64_t output_offset;
+} origami_dz_record;
+
+/* Parses the header of an ORIGQZ1 bundle (the reference's qat_bundle.dz, written at
+ * store.py:694-705) with the checks and messages of qat_deflate_prepare_bundle_dp
+ * (qat_deflate.cpp:1804-1860). records may be null to query the counts only; otherwise
+ * it holds max_records entries. Outputs (nullable): record count, chunk_bytes, total raw
+ * bytes, byte offset of the first compressed chunk. */
+int32_t origami_origqz1_parse(const uint8_t* bundle, int64_t bundle_bytes, origami_dz_record* records,
+                              int64_t max_records, int64_t* num_records, int64_t* chunk_bytes, int64_t* raw_bytes,
+                              int64_t* payload_offset);
+
+/* Upper bound of the raw-deflate size of raw_bytes bytes (zlib compressBound). */
+int64_t origami_deflate_bound(int64_t raw_bytes);
+
+/* Raw deflate (zlib, window bits -15, memory level 8, default strategy; the reference CPU
+ * codec, lossless/cpu_qat.py:64-74) of num_chunks chunks src[src_offsets[i], +src_lengths[i])
+ * into dst at dst_offsets[i], each slot at least origami_deflate_bound(src_lengths[i])
+ * bytes; writes the compressed lengths. `threads` <= 0: all hardware threads. */
+int32_t origami_deflate_chunks(const uint8_t* src, const int64_t* src_offsets, const int64_t* src_lengths,
+                               int64_t num_chunks, int32_t level, uint8_t* dst, int64_t dst_capacity,
+                               const int64_t* dst_offsets, int64_t* dst_lengths, int32_t threads);
+
+/* Raw inflate of num_chunks chunks src[src_offsets[i], +src_lengths[i]) into
+ * dst[dst_offsets[i], +dst_lengths[i]); every chunk must decode to exactly dst_lengths[i]
+ * bytes (lossless/cpu_qat.py:76-84). Replaces the reference's decompress-window + torch.cat
+ * + pageable copy (worker.py:796-1049): dst is the pinned staging the H2D copy reads. */
+int32_t origami_inflate_chunks(const uint8_t* src, const int64_t* src_offsets, const int64_t* src_lengths,
+                               int64_t num_chunks, uint8_t* dst, int64_t dst_capacity, const int64_t* dst_offsets,
+                               const int64_t* dst_lengths, int32_t threads);
 
 #ifdef __cplusplus
 } /* extern "C" */

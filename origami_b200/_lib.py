@@ -104,6 +104,14 @@ def _declare(L: ctypes.CDLL) -> None:
         _vp, i64, i64, i64, i64, i64, i64, i64, i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, i32, P(PagedKV), i32, _vp,
         i64, i64, _vp, _vp]
     L.origami_kivi_dequantize_to_kv_cache.restype = i32
+    L.origami_origqz1_parse.argtypes = [_vp, i64, _vp, i64, _vp, _vp, _vp, _vp]
+    L.origami_origqz1_parse.restype = i32
+    L.origami_deflate_bound.argtypes = [i64]
+    L.origami_deflate_bound.restype = i64
+    L.origami_deflate_chunks.argtypes = [_vp, _vp, _vp, i64, i32, _vp, i64, _vp, _vp, i32]
+    L.origami_deflate_chunks.restype = i32
+    L.origami_inflate_chunks.argtypes = [_vp, _vp, _vp, i64, _vp, i64, _vp, _vp, i32]
+    L.origami_inflate_chunks.restype = i32
 
 
 def lib() -> ctypes.CDLL:
@@ -144,6 +152,10 @@ EXPORTS = (
     "origami_cachegen_unpack_dequantize_to_kv_cache",
     "origami_cachegen_unpack_dequantize",
     "origami_kivi_dequantize_to_kv_cache",
+    "origami_origqz1_parse",
+    "origami_deflate_bound",
+    "origami_deflate_chunks",
+    "origami_inflate_chunks",
 )
 
 ORIGAMI_DTYPE_F16 = 1

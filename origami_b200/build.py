@@ -13,9 +13,9 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 CSRC = HERE / "csrc"
 LIB = HERE / "liborigami_b200.so"
-SOURCES = ["abi.cu", "quant.cu"]
+SOURCES = ["abi.cu", "quant.cu", "host_codec.cpp"]
 # every kernel header and source, plus the public header
-DEPS = sorted(p.name for p in CSRC.iterdir() if p.suffix in (".cu", ".cuh", ".h")) + ["../../include/origami_b200.h"]
+DEPS = sorted(p.name for p in CSRC.iterdir() if p.suffix in (".cu", ".cuh", ".h", ".cpp")) + ["../../include/origami_b200.h"]
 
 NVCC_FLAGS = [
     "-O3",
@@ -45,7 +45,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     if not force and not stale():
         return LIB
     tmp = LIB.with_suffix(".so.tmp")
-    cmd = [nvcc(), *NVCC_FLAGS, "-o", str(tmp), *[str(CSRC / s) for s in SOURCES]]
+    cmd = [nvcc(), *NVCC_FLAGS, "-o", str(tmp), *[str(CSRC / s) for s in SOURCES], "-lz"]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
     subprocess.run(cmd, check=True)

@@ -10,6 +10,12 @@ whatever the model runs on its compute stream. ``wait_for_layer_load`` is a
 stream->event wait, never a host block (the reference blocks on a future and then waits,
 worker.py:553-572).
 
+enqueue_from_bundle is the codec handoff: the host codec decodes a layer's chunks out of
+the ORIGQZ1 bundle straight into a pinned staging slot (one of a ring as deep as the
+device ring), which the copy stream then moves to the device; the reference instead
+concatenates decoded chunks and copies them through pageable memory (worker.py:796-1049,
+benchmark_utils.py:438).
+
 SavePipeline: the mirror image: pack each layer on a save stream into a device slot
 and copy it to pinned host memory on a copy stream, one event per layer for the host
 codec to wait on.
@@ -68,6 +74,36 @@ class RestorePipeline:
         ready = torch.cuda.Event()
         ready.record(self.restore_stream)
         return ready
+
+    def enqueue_from_bundle(self, bundle, layer_name: str, fmt: LayerFormat, kv_layer: torch.Tensor, block_ids,
+                            error_count: torch.Tensor | None = None, *, threads: int = 0) -> torch.cuda.Event:
+        """Host codec -> H2D handoff: decode the layer's chunks from an ORIGQZ1 bundle
+        (origami_b200.bundle.QatBundle) straight into a pinned staging slot at their packed
+        offsets, then enqueue() it. The slot is reused once its previous copy has finished
+        (the only host wait), so decoding layer L+1 overlaps the copy and restore of L."""
+        staging = self._host_slot(fmt.packed_bytes)
+        bundle.inflate_layer_into(layer_name, fmt, staging.buf[: fmt.packed_bytes], threads=threads)
+        ready = self.enqueue(staging.buf, fmt, kv_layer, block_ids, error_count=error_count)
+        staging.copied.record(self.copy_stream)
+        staging.used = True
+        return ready
+
+    def _host_slot(self, n: int) -> _Slot:
+        if not hasattr(self, "_host"):
+            self._host, self._host_next = [], 0
+        if len(self._host) < len(self.slots):
+            size = max(n, self.slots[0].buf.numel())
+            self._host.append(_Slot(torch.empty((size,), dtype=torch.uint8, pin_memory=True), torch.cuda.Event(),
+                                    torch.cuda.Event()))
+            slot = self._host[-1]
+        else:
+            slot = self._host[self._host_next]
+            self._host_next = (self._host_next + 1) % len(self._host)
+            if slot.used:
+                slot.copied.synchronize()  # its bytes have reached the device
+        if slot.buf.numel() < n:
+            raise ValueError("pinned staging slot smaller than the packed layer")
+        return slot
 
     @staticmethod
     def wait_for_layer_load(event: torch.cuda.Event, stream: torch.cuda.Stream | None = None) -> None:

@@ -26,6 +26,7 @@ import numpy as np
 import torch
 
 from origami_b200.lossless.chunking import plan_head_channel_chunks
+from origami_b200.metadata import ChunkLayout
 
 FORMAT_NAME = "origami_planes_v1"
 
@@ -149,6 +150,16 @@ class LayerFormat:
 
     def chunk_views(self, packed: torch.Tensor) -> list[torch.Tensor]:
         return [packed[int(a):int(b)] for a, b in zip(self.offsets[:-1], self.offsets[1:])]
+
+    def chunk_layouts(self) -> list[ChunkLayout]:
+        """ChunkLayout of every chunk k = q * S + s (metadata.py:22-31): spec s of the
+        planner, unpacked_bytes = the chunk's packed byte count (what the codec decodes)."""
+        out = []
+        for k in range(self.num_chunks):
+            h0, h1, c0, c1, t0, t1 = (int(v) for v in self.specs[k % self.num_specs])
+            out.append(ChunkLayout(self.layer_index, h0, h1, c0, c1, t0, t1,
+                                   int(self.offsets[k + 1] - self.offsets[k])))
+        return out
 
     def alloc_packed(self, device: torch.device | str, *, pin: bool = False) -> torch.Tensor:
         """A packed buffer whose allocation extends to a multiple of 16 bytes."""

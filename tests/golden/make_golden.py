@@ -16,6 +16,11 @@ layout helpers) through a package-path shim, runs them on seeded inputs and writ
                        (lossless/cpu_qat.py:64-84), with the input
   select_blocks.npz    the worker's _select_blocks (index_select) on a seeded cache
                        (worker.py:1881-1897)
+  bundle_v1_zlib/, bundle_v1_raw/
+                       bundle_v1 directories (manifest.json, payload.bin and, for the
+                       deflate codec, the ORIGQZ1 qat_bundle.dz) written by the reference's
+                       LocalFileOrigamiStore (store.py:706-867) from seeded chunks, with
+                       the chunk inputs (inputs.npz)
 
 The reference GPU unpack kernel cannot run here; tests/golden/make_ref_vectors.py
 produces its vectors on a B200 from the compiled reference extension.
@@ -136,7 +141,73 @@ def main(root: str) -> None:
     sel_bf = W._select_blocks(W.__new__(W), cache_bf, ids)
     np.savez_compressed(HERE / "select_blocks.npz", cache=cache.numpy(), ids=np.asarray(ids), selected=sel.numpy(),
                         cache_blocks_first=cache_bf.numpy(), selected_blocks_first=sel_bf.numpy())
+    bundle_cases(m, root)
     print("golden fixtures written to", HERE)
+
+
+BUNDLE_LAYERS = ("model.layers.0.self_attn.attn", "model.layers.1.self_attn.attn")
+
+
+def bundle_inputs(case: str):
+    """Seeded chunk inputs of a bundle case: per layer, the raw chunk bytes (a planes-format
+    packed layer of 100 tokens x 2 heads x 16 channels cut by the planner with 1000-byte
+    chunks, so chunk sizes differ) and the chunk layout rows."""
+    sys.path.insert(0, str(HERE.parents[1]))
+    from origami_b200 import LayerFormat
+
+    rng = np.random.default_rng(1234 if case == "zlib" else 4321)
+    layers = BUNDLE_LAYERS if case == "zlib" else BUNDLE_LAYERS[:1]
+    out = {}
+    for li, name in enumerate(layers):
+        fmt = LayerFormat(100, 2, 16, chunk_min_bytes=1000, chunk_target_bytes=1000, chunk_max_bytes=1000,
+                          layer_index=li)
+        raw = (rng.normal(0, 12, fmt.packed_bytes).astype(np.int64) & 0xFF).astype(np.uint8)
+        rows = [[l.layer_index, l.head_start, l.head_end, l.channel_start, l.channel_end, l.token_start,
+                 l.token_end, l.unpacked_bytes] for l in fmt.chunk_layouts()]
+        out[name] = (raw, np.asarray(fmt.offsets, dtype=np.int64), rows, fmt.metadata())
+    return out
+
+
+def bundle_cases(m, root: str) -> None:
+    """bundle_v1 directories written by the reference's LocalFileOrigamiStore
+    (store.py:706-867): a zlib payload of two layers (with ORIGQZ1 qat_bundle.dz) and a
+    raw payload (no ORIGQZ1 file), plus the inputs that built them."""
+    import importlib
+    import shutil
+    import tempfile
+
+    import torch
+
+    st = importlib.import_module(f"{PKG}.store")
+    md = importlib.import_module(f"{PKG}.metadata")
+    codec = m["cpu_qat"].CpuLosslessCodec("zlib")
+    for case in ("zlib", "raw"):
+        inputs = bundle_inputs(case)
+        payload = md.OrigamiPayload(cache_key=f"req-7:{case}/bundle", request_id="req-7", quantizer="origami_planes",
+                                    quantizer_config_hash="cafe01", token_start=0, token_count=100,
+                                    metadata={"model": "synthetic", "layers": len(inputs)})
+        store_arrays = {}
+        for name, (raw, offsets, rows, meta) in inputs.items():
+            chunks = []
+            for k, row in enumerate(rows):
+                data = torch.from_numpy(raw[offsets[k]:offsets[k + 1]].copy())
+                comp = codec._zlib_compress(data) if case == "zlib" else data
+                chunks.append(md.ChunkRecord(chunk_id=k, layout=md.ChunkLayout(*row), codec=case, compressed=comp,
+                                             compressed_bytes=int(comp.numel()), unpacked_bytes=int(data.numel())))
+            # insertion order of chunks is scrambled: the writer sorts them
+            chunks = chunks[1::2] + chunks[0::2]
+            payload.layer_payloads[name] = md.LayerPayload(layer_name=name, quantizer="origami_planes",
+                                                           quant_metadata=meta, chunks=chunks)
+            store_arrays[f"{name}/raw"] = raw
+            store_arrays[f"{name}/offsets"] = offsets
+        with tempfile.TemporaryDirectory() as tmp:
+            st.LocalFileOrigamiStore(tmp).put(payload)
+            src = Path(tmp) / st._safe_key(payload.cache_key)
+            dst = HERE / f"bundle_v1_{case}"
+            if dst.exists():
+                shutil.rmtree(dst)
+            shutil.copytree(src, dst)
+        np.savez_compressed(HERE / f"bundle_v1_{case}" / "inputs.npz", **store_arrays)
 
 
 if __name__ == "__main__":
