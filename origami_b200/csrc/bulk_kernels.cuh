@@ -112,7 +112,10 @@ __global__ void __launch_bounds__(kThreads, 2) restore_bulk(const __grid_constan
   __syncthreads();
 
   // Every thread arrives once per stage use (announcing its own bytes) and issues the
-  // bulk copies of its run rows; words past the buffer end are read bytewise.
+  // bulk copies of its run rows; words past the buffer end are read bytewise. The tile's
+  // block-table rows go to registers and are written to its stage after the current
+  // tile's work.
+  RowoffRegs<BG::TT> next_rows;
   auto issue = [&](int s, int tile) {
     const TmaTile t = bulk_tile<BG::TT>(args, tile);
     uint8_t* sb = smem + s * BG::stage_bytes;
@@ -153,7 +156,7 @@ __global__ void __launch_bounds__(kThreads, 2) restore_bulk(const __grid_constan
         *reinterpret_cast<uint4*>(row + 16 * w) = make_uint4(v[0], v[1], v[2], v[3]);
       }
     }
-    bulk_rowoff<BG::TT>(args, t, reinterpret_cast<int64_t*>(sb + BG::stage_bytes - BG::rowoff_bytes));
+    rowoff_load<BG::TT>(args, t, next_rows);
   };
 
   const int per = args.num_tiles / static_cast<int>(gridDim.x);
@@ -161,7 +164,10 @@ __global__ void __launch_bounds__(kThreads, 2) restore_bulk(const __grid_constan
   const int first = static_cast<int>(blockIdx.x) * per + min(static_cast<int>(blockIdx.x), extra);
   const int last = first + per + (static_cast<int>(blockIdx.x) < extra ? 1 : 0);
   int tile = first;
-  if (tile < last) issue(0, tile);
+  if (tile < last) {
+    issue(0, tile);
+    rowoff_store<BG::TT>(args.err, next_rows, reinterpret_cast<int64_t*>(smem + BG::stage_bytes - BG::rowoff_bytes));
+  }
   uint32_t phases = 0u;
   const int a = tid % G::A;
   const int o = tid / G::A;
@@ -249,6 +255,9 @@ __global__ void __launch_bounds__(kThreads, 2) restore_bulk(const __grid_constan
       st_global_cs16(rows + (off + 8 * oc) * 2,
                      *reinterpret_cast<const uint4*>(rows_sm + r * (D * 2) + ((oc + (r >> 3)) & (G::O - 1)) * 16));
     }
+    if (next < last)
+      rowoff_store<BG::TT>(args.err, next_rows,
+                           reinterpret_cast<int64_t*>(smem + (s ^ 1) * BG::stage_bytes + BG::stage_bytes - BG::rowoff_bytes));
     __syncthreads();
   }
 }

@@ -184,6 +184,8 @@ int32_t origami_cachegen_unpack_dequantize_to_kv_cache(
   a.heads = static_cast<int32_t>(cache->num_heads);
   const int64_t C = cache->num_heads * cache->head_dim;
   if (C > 0x7FFFFFFF) return fail(ORIGAMI_ERR_UNSUPPORTED, "heads * head_dim must be below 2^31");
+  if (tokens > 0x7FFFFFFF || cache->block_size > 0x7FFFFFFF)
+    return fail(ORIGAMI_ERR_UNSUPPORTED, "tokens and block_size must be below 2^31");
   a.C = static_cast<int32_t>(C);
   const bool vec = C % 8 == 0 && aligned(cache->d_data, 16);
   a.nvec = vec ? static_cast<int32_t>(C / 8) : a.C;

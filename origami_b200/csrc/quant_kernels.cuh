@@ -141,13 +141,32 @@ __device__ __forceinline__ void cg_table(float (*table)[256], const int64_t* bin
   __syncthreads();
 }
 
-// A warp per (kv, token) row. VEC: eight symbols -> one 16-byte store; a lane first issues
-// the loads of up to kCgUnroll vectors (and the row's block id and max), then dequantizes
-// and stores them, so several loads are in flight per lane.
-constexpr int kCgUnroll = 4;
+// Eight b-bit symbols of a 64-bit field -> eight output elements looked up by warp shuffle:
+// lane l holds `lut`, the finished 16-bit element for symbol value l (b <= 5). All 32 lanes
+// must execute it.
+__device__ __forceinline__ uint4 lookup8_shfl(uint32_t lut, uint64_t field, int bits) {
+  const uint32_t mask = (1u << bits) - 1u;
+  const uint32_t w[2] = {static_cast<uint32_t>(field), static_cast<uint32_t>(field >> (4 * bits))};
+  uint32_t o[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t x = w[j >> 1];
+    const int k = 2 * (j & 1);
+    const uint32_t e0 = __shfl_sync(0xFFFFFFFFu, lut, static_cast<int>((x >> (k * bits)) & mask));
+    const uint32_t e1 = __shfl_sync(0xFFFFFFFFu, lut, static_cast<int>((x >> ((k + 1) * bits)) & mask));
+    o[j] = __byte_perm(e0, e1, 0x5410);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
 
+// A warp per (kv, token) row; VEC: eight symbols -> one 16-byte store per lane step.
+// Symbols of up to 5 bits (every CacheGen bins setting of the reference,
+// cachegen_adapter.py:49-57) are dequantized by shuffle: each lane computes the finished
+// element for one symbol value, ((v - c) / c) * max then the output rounding, exactly as the
+// reference does per element, and the other lanes fetch it. Wider symbols go through the
+// shared-memory quotient table, a multiply and a conversion per element.
 template <typename MAXT, typename OUT, bool VEC>
-__global__ void __launch_bounds__(kThreads, 5) cachegen_to_cache(const __grid_constant__ CgArgs a) {
+__global__ void __launch_bounds__(kThreads) cachegen_to_cache(const __grid_constant__ CgArgs a) {
   __shared__ float table[2][256];
   cg_table(table, a.bins);
   const int lane = threadIdx.x & 31;
@@ -156,46 +175,36 @@ __global__ void __launch_bounds__(kThreads, 5) cachegen_to_cache(const __grid_co
   for (int64_t row = blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); row < rows; row += warps) {
     const int kv = row >= a.tokens ? 1 : 0;
     const int64_t t = row - kv * a.tokens;
-    const int64_t bi = t / a.block_size;
-    const float* q = table[kv];
+    const int64_t bi = static_cast<int32_t>(t) / static_cast<int32_t>(a.block_size);
     const uint8_t* s = a.stream[kv];
     const int64_t nb = a.stream_bytes[kv];
     const int bits = a.bits[kv];
+    const float m = to_f32(static_cast<const MAXT*>(a.maxv[kv])[t]);
+    const int64_t blk = a.ids[bi];
+    if (blk < 0 || blk >= a.num_blocks) {  // counted per (kv, token, head) row
+      if (lane == 0 && a.err) atomicAdd(a.err, static_cast<uint32_t>(a.heads));
+      continue;
+    }
+    OUT* dst = reinterpret_cast<OUT*>(a.cache) + kv * a.kv_stride + blk * a.block_stride +
+               (t - bi * a.block_size) * a.token_stride;
     if constexpr (VEC) {
-      for (int v0 = 0; v0 < a.nvec; v0 += 32 * kCgUnroll) {
-        uint64_t raw[kCgUnroll];
-#pragma unroll
-        for (int u = 0; u < kCgUnroll; ++u) {
-          const int v = v0 + lane + 32 * u;
-          raw[u] = v < a.nvec ? symbols8_raw(s, nb, t * a.nvec + v, bits) : 0;
+      if (bits <= 5) {
+        const uint32_t lut = out_bits<OUT>(table[kv][lane] * m);
+        for (int v0 = 0; v0 < a.nvec; v0 += 32) {
+          const int v = v0 + lane;
+          const uint64_t field = v < a.nvec ? symbols8_raw(s, nb, t * a.nvec + v, bits) : 0;
+          const uint4 out = lookup8_shfl(lut, field, bits);
+          if (v < a.nvec) st_global_cs16(dst + 8 * v, out);
         }
-        const int64_t blk = a.ids[bi];
-        const float m = to_f32(static_cast<const MAXT*>(a.maxv[kv])[t]);
-        if (blk < 0 || blk >= a.num_blocks) break;
-        OUT* dst = reinterpret_cast<OUT*>(a.cache) + kv * a.kv_stride + blk * a.block_stride +
-                   (t - bi * a.block_size) * a.token_stride;
-#pragma unroll
-        for (int u = 0; u < kCgUnroll; ++u) {
-          const int v = v0 + lane + 32 * u;
-          if (v >= a.nvec) break;
-          st_global_cs16(dst + 8 * v, dequant8<OUT>(q, m, raw[u], bits));
-        }
+      } else {
+        for (int v = lane; v < a.nvec; v += 32)
+          st_global_cs16(dst + 8 * v, dequant8<OUT>(table[kv], m, symbols8_raw(s, nb, t * a.nvec + v, bits), bits));
       }
     } else {
-      const int64_t blk = a.ids[bi];
-      if (blk >= 0 && blk < a.num_blocks) {
-        OUT* dst = reinterpret_cast<OUT*>(a.cache) + kv * a.kv_stride + blk * a.block_stride +
-                   (t - bi * a.block_size) * a.token_stride;
-        const float m = to_f32(static_cast<const MAXT*>(a.maxv[kv])[t]);
-        for (int c = lane; c < a.C; c += 32) {
-          const uint32_t sym = symbol_at(s, nb, t * a.C + c, bits);
-          reinterpret_cast<uint16_t*>(dst)[c] = static_cast<uint16_t>(out_bits<OUT>(q[sym] * m));
-        }
+      for (int c = lane; c < a.C; c += 32) {
+        const uint32_t sym = symbol_at(s, nb, t * a.C + c, bits);
+        reinterpret_cast<uint16_t*>(dst)[c] = static_cast<uint16_t>(out_bits<OUT>(table[kv][sym] * m));
       }
-    }
-    if (lane == 0 && a.err) {  // counted per (kv, token, head) row
-      const int64_t blk = a.ids[bi];
-      if (blk < 0 || blk >= a.num_blocks) atomicAdd(a.err, static_cast<uint32_t>(a.heads));
     }
   }
 }
@@ -246,8 +255,18 @@ __global__ void __launch_bounds__(kThreads) cachegen_unpack(const __grid_constan
     __half* dst = a.out + (((layer * 2 + kv) * a.heads + h) * a.tokens + t) * a.head_dim;
     if constexpr (VEC) {
       const int64_t k0 = (t * C + h * a.head_dim) >> 3;
-      for (int v = lane; v < a.head_dim / 8; v += 32) {
-        st_global_cs16(dst + 8 * v, dequant8<__half>(table, m, symbols8_raw(s, nb, k0 + v, bits), bits));
+      const int nvec = static_cast<int>(a.head_dim / 8);
+      if (bits <= 5) {
+        const uint32_t lut = out_bits<__half>(table[lane] * m);
+        for (int v0 = 0; v0 < nvec; v0 += 32) {
+          const int v = v0 + lane;
+          const uint64_t field = v < nvec ? symbols8_raw(s, nb, k0 + v, bits) : 0;
+          const uint4 out = lookup8_shfl(lut, field, bits);
+          if (v < nvec) st_global_cs16(dst + 8 * v, out);
+        }
+      } else {
+        for (int v = lane; v < nvec; v += 32)
+          st_global_cs16(dst + 8 * v, dequant8<__half>(table, m, symbols8_raw(s, nb, k0 + v, bits), bits));
       }
     } else {
       for (int64_t d = lane; d < a.head_dim; d += 32) {
@@ -334,6 +353,12 @@ __global__ void __launch_bounds__(kThreads) kivi_to_cache_elem(const __grid_cons
 // x O channel octets (O = D / 8 divides 256, TT = 8 * A). Needs sink_tokens % 8 == 0 so a
 // token octet is all sink or all body. UNI (group_size % 8 == 0): the value group of a
 // channel octet and the key group of a token octet are single groups.
+// Eight META values as one 16-byte-aligned vector access.
+template <typename META>
+struct alignas(16) VecOf {
+  META v[8];
+};
+
 // Shared memory: [runs: D rows x rs][bit0: D x int32][rowoff: TT x int64][token rows]
 // [scale, zero: kMetaSlots x max(TT, D) META each]. The staged-run row holds up to TT
 // bytes (8-bit symbols) plus word slack; its stride is not a multiple of 128 bytes at
@@ -419,27 +444,29 @@ __global__ void __launch_bounds__(kThreads) kivi_to_cache(const __grid_constant_
     // kMetaSlots value groups (one token's slots per row) or key groups (one group's D
     // channels per row); otherwise phase B reads them from global memory.
     bool staged = false;
-    int64_t mbase = 0;  // first staged value group / key group
+    int mbase = 0;  // first staged value group / key group
     if constexpr (UNI) {
       if (nbody > 0) {
         const META* sc = static_cast<const META*>(a.scale[kv]);
         const META* ze = static_cast<const META*>(a.zero[kv]);
         if (kv) {
-          mbase = static_cast<int64_t>(h) * D / a.group_size;
-          const int ng = static_cast<int>((static_cast<int64_t>(h) * D + D - 1) / a.group_size - mbase + 1);
+          // (channel and token counts are below 2^31, checked on the host: 32-bit divisions)
+          mbase = h * D / static_cast<int>(a.group_size);
+          const int ng = static_cast<int>((h * D + D - 1) / static_cast<int>(a.group_size) - mbase + 1);
           if (ng <= kMetaSlots) {
             staged = true;
+            // [group][token]: a thread's eight tokens of one group are one vector
             for (int i = tid; i < nbody * ng; i += kThreads) {
               const int r = i / ng;
               const int g = i - r * ng;
               const int64_t idx = (tb0 - a.sink_tokens + r) * a.value_groups + mbase + g;
-              msc[r * kMetaSlots + g] = sc[idx];
-              mze[r * kMetaSlots + g] = ze[idx];
+              msc[g * G::TT + r] = sc[idx];
+              mze[g * G::TT + r] = ze[idx];
             }
           }
         } else {
-          mbase = (tb0 - a.sink_tokens) / a.group_size;
-          const int nkg = static_cast<int>((tb1 - 1 - a.sink_tokens) / a.group_size - mbase + 1);
+          mbase = static_cast<int>(tb0 - a.sink_tokens) / static_cast<int>(a.group_size);
+          const int nkg = static_cast<int>(tb1 - 1 - a.sink_tokens) / static_cast<int>(a.group_size) - mbase + 1;
           if (nkg <= kMetaSlots) {
             staged = true;
             for (int i = tid; i < nkg * D; i += kThreads) {
@@ -489,20 +516,24 @@ __global__ void __launch_bounds__(kThreads) kivi_to_cache(const __grid_constant_
           const META* sc = static_cast<const META*>(a.scale[kv]);
           const META* ze = static_cast<const META*>(a.zero[kv]);
           if (kv) {
-            const int64_t g = ch0 / a.group_size;
+            const int g = static_cast<int>(ch0) / static_cast<int>(a.group_size);
+            META vs[8], vz[8];
+            if (staged) {  // tokens k0 .. k0 + 7 of group g (k0 % 8 == 0): one vector each
+              const int base = (g - mbase) * G::TT + k0;
+              *reinterpret_cast<VecOf<META>*>(vs) = *reinterpret_cast<const VecOf<META>*>(msc + base);
+              *reinterpret_cast<VecOf<META>*>(vz) = *reinterpret_cast<const VecOf<META>*>(mze + base);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const int64_t idx = min64(bq + i, a.body_tokens - 1) * a.value_groups + g;
+                vs[i] = sc[idx];
+                vz[i] = ze[idx];
+              }
+            }
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-              float fs, fz;
-              if (staged) {
-                const int r = min(k0 + i, nbody - 1);
-                const int slot = r * kMetaSlots + static_cast<int>(g - mbase);
-                fs = to_f32(msc[slot]);
-                fz = to_f32(mze[slot]);
-              } else {
-                const int64_t idx = min64(bq + i, a.body_tokens - 1) * a.value_groups + g;
-                fs = to_f32(sc[idx]);
-                fz = to_f32(ze[idx]);
-              }
+              const float fs = to_f32(vs[i]);
+              const float fz = to_f32(vz[i]);
 #pragma unroll
               for (int j = 0; j < 4; ++j) {
                 const uint32_t w = j < 2 ? lo[i] : hi[i];
@@ -514,7 +545,7 @@ __global__ void __launch_bounds__(kThreads) kivi_to_cache(const __grid_constant_
           } else {
             float fs[8], fz[8];
             if (staged) {
-              const int base = static_cast<int>(bq / a.group_size - mbase) * D + 8 * o;
+              const int base = (static_cast<int>(bq) / static_cast<int>(a.group_size) - mbase) * D + 8 * o;
 #pragma unroll
               for (int j = 0; j < 8; ++j) {
                 fs[j] = to_f32(msc[base + j]);

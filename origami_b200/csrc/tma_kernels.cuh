@@ -107,6 +107,50 @@ __device__ __forceinline__ void tma_rowoff(const TmaArgs& a, const TmaTile& t, i
   }
 }
 
+// The same offsets in two halves, so the block-table loads of the next tile overlap the
+// current tile's work: rowoff_load issues them into registers, rowoff_store writes
+// them to shared memory later (-2 marks an invalid block id until it is counted there).
+template <int TT>
+struct RowoffRegs {
+  static constexpr int kPer = (TT + kThreads - 1) / kThreads;
+  int64_t v[kPer];
+};
+
+template <int TT, typename Args, typename Tile>
+__device__ __forceinline__ void rowoff_load(const Args& a, const Tile& t, RowoffRegs<TT>& r) {
+  const int32_t bs = static_cast<int32_t>(a.block_size);
+#pragma unroll
+  for (int k = 0; k < RowoffRegs<TT>::kPer; ++k) {
+    const int i = static_cast<int>(threadIdx.x) + k * kThreads;
+    int64_t off = -1;
+    if (i < TT && i < t.n) {
+      const int32_t tg = static_cast<int32_t>(t.t0) + i;
+      const int32_t bi = tg / bs;
+      const int64_t blk = a.block_ids[t.job][bi];
+      off = (blk < 0 || blk >= a.num_blocks)
+                ? -2
+                : t.kv * a.kv_stride + blk * a.block_stride + static_cast<int64_t>(tg - bi * bs) * a.token_stride +
+                      static_cast<int64_t>(t.h) * a.head_stride;
+    }
+    r.v[k] = off;
+  }
+}
+
+template <int TT>
+__device__ __forceinline__ void rowoff_store(uint32_t* err, RowoffRegs<TT>& r, int64_t* rowoff) {
+#pragma unroll
+  for (int k = 0; k < RowoffRegs<TT>::kPer; ++k) {
+    const int i = static_cast<int>(threadIdx.x) + k * kThreads;
+    if (i < TT) {
+      if (r.v[k] == -2) {
+        if (err) atomicAdd(err, 1u);
+        r.v[k] = -1;
+      }
+      rowoff[i] = r.v[k];
+    }
+  }
+}
+
 template <int MODE, int D>
 struct TmaGeo {
   static constexpr int TT = tile_tokens_for(D);
@@ -155,6 +199,9 @@ __global__ void __launch_bounds__(kThreads) restore_tma(const __grid_constant__ 
   }
   __syncthreads();
 
+  // The next tile's runs come by TMA; its block-table rows are loaded into registers here
+  // and written to its stage after the current tile's work (rowoff_store).
+  RowoffRegs<G::TT> next_rows;
   auto issue = [&](int s, int tile) {
     const TmaTile t = tma_tile<G::TT>(args, tile);
     if (tid == 0) {
@@ -165,11 +212,14 @@ __global__ void __launch_bounds__(kThreads) restore_tma(const __grid_constant__ 
                     static_cast<int32_t>(t.t0 * G::bits(p) / 8), t.h * D, t.job, &bars[s]);
       }
     }
-    tma_rowoff<G::TT>(args, t, reinterpret_cast<int64_t*>(smem + s * G::stage_bytes + G::in_bytes));
+    rowoff_load<G::TT>(args, t, next_rows);
   };
 
   int tile = blockIdx.x;
-  if (tile < args.num_tiles) issue(0, tile);
+  if (tile < args.num_tiles) {
+    issue(0, tile);
+    rowoff_store<G::TT>(args.err, next_rows, reinterpret_cast<int64_t*>(smem + G::in_bytes));
+  }
   uint32_t phases = 0u;  // bit s = parity to wait for on stage s
   const int a = tid % G::A;
   const int o = tid / G::A;
@@ -261,7 +311,9 @@ __global__ void __launch_bounds__(kThreads) restore_tma(const __grid_constant__ 
       st_global_cs16(rows + (off + 8 * oc) * 2,
                      *reinterpret_cast<const uint4*>(rows_sm + r * (D * 2) + ((oc + (r >> 3)) & (G::O - 1)) * 16));
     }
-    __syncthreads();  // stage s and the row buffer are free again
+    if (next < args.num_tiles)
+      rowoff_store<G::TT>(args.err, next_rows, reinterpret_cast<int64_t*>(smem + (s ^ 1) * G::stage_bytes + G::in_bytes));
+    __syncthreads();  // stage s and the row buffer are free again; stage s ^ 1's rows are written
   }
 }
 
