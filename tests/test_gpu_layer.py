@@ -88,8 +88,10 @@ def test_fp16_cache_roundtrip(cuda):
     assert torch.equal(fresh.cpu()[:, blk, t % bs].view(torch.int16), cache[:, blk, t % bs].view(torch.int16))
 
 
-def test_bad_block_ids_are_counted_and_skipped(cuda):
-    T, bs, H, D = 64, 16, 2, 64
+@pytest.mark.parametrize("geom", [(64, 16, 2, 64), (64, 16, 2, 128), (128, 16, 8, 128)],
+                         ids=["h2_d64", "h2_d128", "h8_d128"])
+def test_bad_block_ids_are_counted_and_skipped(cuda, geom):
+    T, bs, H, D = geom
     cache, ids = make_cache(T, bs, H, D, True, seed=11)
     fmt = LayerFormat(T, H, D, BYTE_PLANES)
     d = cache.to(cuda)
@@ -100,7 +102,7 @@ def test_bad_block_ids_are_counted_and_skipped(cuda):
     fresh = torch.zeros_like(d)
     restore_layer(packed, fmt, fresh, bad, error_count=err)
     assert int(err.item()) == 2 * H * bs  # every (kv, head, token) row of the bad block
-    good = [0, 1, 3]
+    good = [b for b in range(T // bs) if b != 2]
     t = torch.cat([torch.arange(b * bs, (b + 1) * bs) for b in good])
     blk = ids[t // bs]
     assert torch.equal(fresh.cpu()[:, blk, t % bs], cache[:, blk, t % bs])
