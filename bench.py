@@ -178,15 +178,17 @@ def measured_hbm_peak():
     return 6650.0, "fallback"
 
 
-def profiled_traffic(kernel: str, workload: str):
-    """dram read+write bytes per launch from the committed ncu summary, if any."""
+def profiled_traffic(kernel: str, workload: str, jobs_per_launch: float):
+    """DRAM read+write bytes per launch: the committed ncu figure per job (one layer of
+    one request; the traffic of a launch grows in proportion to its jobs) times the
+    jobs one launch restores or packs."""
     p = REPO / "profiles" / "traffic.txt"
     if not p.exists():
         return None
     for line in p.read_text().splitlines():
         parts = line.split()
         if len(parts) >= 3 and parts[0] == kernel and parts[1] == workload:
-            return int(parts[2])
+            return int(round(int(parts[2]) * jobs_per_launch))
     return None
 
 
@@ -424,17 +426,18 @@ def run_origami(args, rank, world, local):
     kinds = {fused_kernel_name(f, True) for f in wl.fmts}
     k_restore = "/".join(sorted(kinds))
     k_pack = "/".join(sorted({fused_kernel_name(f, False) for f in wl.fmts}))
+    jobs_per_launch = sum(len(jobs) for _, jobs, _ in wl.groups) / launches
     workload_name = (f"C2_restore_T{wl.tokens[0]}_H{wl.heads}_D{wl.cfg.head_dim}_{wl.planes.name}"
                      if args.config == "C2" and args.chunk_bytes == 1 << 20 and not args.tokens else None)
     roof_restore = {"kernel": k_restore, "bound": "hbm", "achieved": round(achieved_restore, 1), "peak": peak,
                     "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved_restore / peak, 4),
-                    "traffic": profiled_traffic(k_restore, workload_name) if workload_name else None,
+                    "traffic": profiled_traffic(k_restore, workload_name, jobs_per_launch) if workload_name else None,
                     "algorithmic_bytes_per_launch": alg_step // launches,
                     "launch_ms": round(restore_sum / launches, 5),
                     "host_us_per_call": round(host_us_per_call[0 if not primary_pack else 1], 1)}
     roof_pack = {"kernel": k_pack, "bound": "hbm", "achieved": round(achieved_pack, 1), "peak": peak,
                  "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved_pack / peak, 4),
-                 "traffic": profiled_traffic(k_pack, workload_name) if workload_name else None,
+                 "traffic": profiled_traffic(k_pack, workload_name, jobs_per_launch) if workload_name else None,
                  "algorithmic_bytes_per_launch": alg_step // launches,
                  "launch_ms": round(pack_sum / launches, 5)}
 

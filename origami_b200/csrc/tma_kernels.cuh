@@ -179,6 +179,64 @@ struct TmaGeo {
   static constexpr int smem_bytes = 2 * stage_bytes + rows_bytes + 16 + 128;
 };
 
+// Phase B of the restore kernels: thread (a, o) merges the planes of tokens 8a..8a+7 x
+// channels 8o..8o+7 of one staged tile into out[token][4 words] (8 16-bit elements).
+template <int MODE, int D>
+__device__ __forceinline__ void tma_merge(const uint8_t* stage, int a, int o, uint32_t (&out)[8][4]) {
+  using G = TmaGeo<MODE, D>;
+  uint32_t keep_lo[8], keep_hi[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) out[i][0] = out[i][1] = out[i][2] = out[i][3] = 0u;
+#pragma unroll
+  for (int p = 0; p < G::P; ++p) {
+    const int bits = G::bits(p);
+    const int rb = G::run_bytes(p);
+    const uint8_t* pbase = stage + G::plane_off(p);
+    uint32_t lo[8], hi[8];
+#pragma unroll
+    for (int jj = 0; jj < 8; ++jj) {
+      const uint8_t* row = pbase + (8 * o + jj) * rb;
+      if (bits == 8) {
+        const uint2 v = *reinterpret_cast<const uint2*>(row + 8 * a);
+        lo[jj] = v.x;
+        hi[jj] = v.y;
+      } else {
+        // 8 symbols = `bits` bytes at byte a*bits (runs are 16-byte aligned rows)
+        uint32_t v0, v1;
+        window64(row, 8 * a * bits, v0, v1);
+        spread8_rt(v0, v1, bits, lo[jj], hi[jj]);
+      }
+    }
+    transpose8x8(lo, hi);
+    if constexpr (MODE == kModeByte2) {
+      if (p == 0) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          keep_lo[i] = lo[i];
+          keep_hi[i] = hi[i];
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          out[i][0] = prmt(lo[i], keep_lo[i], 0x5140);
+          out[i][1] = prmt(lo[i], keep_lo[i], 0x7362);
+          out[i][2] = prmt(hi[i], keep_hi[i], 0x5140);
+          out[i][3] = prmt(hi[i], keep_hi[i], 0x7362);
+        }
+      }
+    } else {
+      const int sh = G::shift(p);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        out[i][0] |= prmt(lo[i], 0u, 0x4140) << sh;
+        out[i][1] |= prmt(lo[i], 0u, 0x4342) << sh;
+        out[i][2] |= prmt(hi[i], 0u, 0x4140) << sh;
+        out[i][3] |= prmt(hi[i], 0u, 0x4342) << sh;
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------------------
 // restore_tma
 // ---------------------------------------------------------------------------------------
@@ -241,59 +299,7 @@ __global__ void __launch_bounds__(kThreads) restore_tma(const __grid_constant__ 
 
     // Phase B: 8 tokens x 8 channels per thread, planes merged in registers.
     uint32_t out[8][4];
-    uint32_t keep_lo[8], keep_hi[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) out[i][0] = out[i][1] = out[i][2] = out[i][3] = 0u;
-#pragma unroll
-    for (int p = 0; p < G::P; ++p) {
-      constexpr int unused = 0;
-      (void)unused;
-      const int bits = G::bits(p);
-      const int rb = G::run_bytes(p);
-      const uint8_t* pbase = smem + s * G::stage_bytes + G::plane_off(p);
-      uint32_t lo[8], hi[8];
-#pragma unroll
-      for (int jj = 0; jj < 8; ++jj) {
-        const uint8_t* row = pbase + (8 * o + jj) * rb;
-        if (bits == 8) {
-          const uint2 v = *reinterpret_cast<const uint2*>(row + 8 * a);
-          lo[jj] = v.x;
-          hi[jj] = v.y;
-        } else {
-          // 8 symbols = `bits` bytes at byte a*bits (runs are 16-byte aligned rows)
-          uint32_t v0, v1;
-          window64(row, 8 * a * bits, v0, v1);
-          spread8_rt(v0, v1, bits, lo[jj], hi[jj]);
-        }
-      }
-      transpose8x8(lo, hi);
-      if constexpr (MODE == kModeByte2) {
-        if (p == 0) {
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            keep_lo[i] = lo[i];
-            keep_hi[i] = hi[i];
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            out[i][0] = prmt(lo[i], keep_lo[i], 0x5140);
-            out[i][1] = prmt(lo[i], keep_lo[i], 0x7362);
-            out[i][2] = prmt(hi[i], keep_hi[i], 0x5140);
-            out[i][3] = prmt(hi[i], keep_hi[i], 0x7362);
-          }
-        }
-      } else {
-        const int sh = G::shift(p);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          out[i][0] |= prmt(lo[i], 0u, 0x4140) << sh;
-          out[i][1] |= prmt(lo[i], 0u, 0x4342) << sh;
-          out[i][2] |= prmt(hi[i], 0u, 0x4140) << sh;
-          out[i][3] |= prmt(hi[i], 0u, 0x4342) << sh;
-        }
-      }
-    }
+    tma_merge<MODE, D>(smem + s * G::stage_bytes, a, o, out);
     // Token rows to shared memory (the previous tile's phase C finished at the loop-end barrier).
     const int phys = (o + a) & (G::O - 1);
 #pragma unroll

@@ -26,6 +26,11 @@ GEOMS = [
     (20000, 16, 8, 128, 1 << 20),
     (30000, 32, 4, 64, 1 << 18),
     (12345, 16, 4, 256, 1 << 20),
+    # TMA kernels over odd, 6 and 16 heads, and D = 256 with 8 heads
+    (1024, 16, 3, 128, 1 << 20),
+    (2048, 16, 6, 64, 1 << 20),
+    (512, 16, 16, 128, 1 << 20),
+    (256, 16, 8, 256, 1 << 20),
 ]
 PLANES = [BYTE_PLANES, BF16_BIT_PLANES, FP16_BIT_PLANES, ODD_PLANES]
 
@@ -88,8 +93,9 @@ def test_fp16_cache_roundtrip(cuda):
     assert torch.equal(fresh.cpu()[:, blk, t % bs].view(torch.int16), cache[:, blk, t % bs].view(torch.int16))
 
 
-@pytest.mark.parametrize("geom", [(64, 16, 2, 64), (64, 16, 2, 128), (128, 16, 8, 128)],
-                         ids=["h2_d64", "h2_d128", "h8_d128"])
+@pytest.mark.parametrize("geom", [(64, 16, 2, 64), (64, 16, 2, 128), (128, 16, 8, 128), (128, 16, 3, 128),
+                                  (256, 16, 4, 64)],
+                         ids=["h2_d64", "h2_d128", "h8_d128", "h3_d128", "h4_d64"])
 def test_bad_block_ids_are_counted_and_skipped(cuda, geom):
     T, bs, H, D = geom
     cache, ids = make_cache(T, bs, H, D, True, seed=11)
