@@ -264,6 +264,36 @@ int32_t origami_kivi_dequantize_to_kv_cache(
     const origami_paged_kv* cache, int32_t cache_dtype, const int64_t* d_block_ids, int64_t num_block_ids,
     int64_t tokens, uint32_t* d_error_count, origami_stream_t stream);
 
+/* Drop-in for fused_prefix_attention_cuda (bitpack_layout_cuda.cpp:716-890, kernel
+ * bitpack_layout_cuda.cu:873-1091; called through native_gpu.py:279-420). Attention of
+ * query [query_tokens, query_heads, 128] (query_dtype F16 or BF16; d_output the same) over
+ * keys [0, min(sequence_length - 1, query_start_position + q)] for query token q: keys
+ * below prefix_tokens from the KIVI (codec 0) or KVQuant (codec 1) symbol streams and fp16
+ * metadata (meta_numel = element counts of key_scale, key_zero, value_scale, value_zero,
+ * key_sink, value_sink), the others from the paged cache through the int32 block table
+ * (an out-of-range block reads as zero K and V). 3-bit symbols are nibble-packed; 2, 4 and
+ * 8 bits are dense. Same checks and messages as the reference.
+ * d_workspace: origami_fused_prefix_attention_workspace() bytes, 16-byte aligned and zero
+ * before its first use (the kernel leaves it zero again); calls sharing a workspace must
+ * not overlap. d_error_flags (nullable) gets bit 31 if a bounded wait inside the kernel
+ * ran out. */
+int32_t origami_fused_prefix_attention(
+    const uint8_t* d_bytestream, int64_t bytestream_bytes, int64_t key_offset, int64_t key_bytes,
+    int64_t value_offset, int64_t value_bytes, int64_t codec, int64_t bits, int64_t group_size, int64_t sink_tokens,
+    const void* d_key_scale, const void* d_key_zero, const void* d_value_scale, const void* d_value_zero,
+    const void* d_key_sink, const void* d_value_sink, const int64_t* meta_numel, int32_t meta_dtype,
+    const void* d_query, int32_t query_dtype, int64_t query_tokens, int64_t query_heads, int64_t head_dim,
+    const origami_paged_kv* cache, int32_t cache_dtype, const int32_t* d_block_table, int64_t block_table_len,
+    int64_t prefix_tokens, int64_t query_start_position, int64_t sequence_length, double softmax_scale,
+    void* d_output, void* d_workspace, int64_t workspace_bytes, uint32_t* d_error_flags, origami_stream_t stream);
+
+/* Workspace bytes origami_fused_prefix_attention needs for these shapes on the current
+ * device (0 when the key range is not split). No counterpart in the reference, whose
+ * kernel needs no workspace (one CTA per query token and head). */
+int32_t origami_fused_prefix_attention_workspace(int64_t query_tokens, int64_t query_heads, int64_t kv_heads,
+                                                 int64_t query_start_position, int64_t sequence_length,
+                                                 int64_t* workspace_bytes);
+
 /* ---------------------------------------------------------------------------------
  * Host codec boundary (CPU only; no CUDA calls): the ORIGQZ1 chunk bundle and raw-deflate
  * chunk coding between caller-owned host buffers (pinned staging on the restore path)

@@ -494,3 +494,145 @@ int64_t oracle_kivi_to_cache(const uint8_t* bytestream, int64_t bytestream_bytes
   }
   return skipped;
 }
+
+/* ---- fused prefix attention (cu:853-1091, cpp:716-890) ---------------------------- */
+
+/* origami_fused_unpack_symbol (cu:853-871): 3-bit symbols are two nibbles per byte, low
+ * nibble first; the other widths are dense (unpack_symbol_direct). */
+static uint32_t fused_symbol(const uint8_t* src, int64_t src_bytes, int64_t index, int bits) {
+  if (bits == 3) {
+    const int64_t byte = index >> 1;
+    if (byte >= src_bytes) return 0u;
+    return (uint32_t)((src[byte] >> ((index & 1) * 4)) & 0x07);
+  }
+  return symbol_direct(src, src_bytes, index, bits);
+}
+
+typedef struct {
+  const uint8_t* bytestream;
+  int64_t key_offset, key_bytes, value_offset, value_bytes;
+  int codec, bits;
+  int64_t group_size, sink_tokens, prefix_tokens;
+  const uint16_t *key_scale, *key_zero, *value_scale, *value_zero, *key_sink, *value_sink;
+  const uint16_t* kv_cache;
+  int cache_bf16, blocks_first;
+  int64_t num_cache_blocks, block_size, kv_heads;
+  const int32_t* block_table;
+} fused_src;
+
+static float h2f(uint16_t h) { return oracle_half_to_float(h); }
+
+/* One K (kv = 0) or V (kv = 1) element as the reference kernel reads it (cu:936-972 and
+ * 1017-1069), in fp32; s * scale + zero contracts to one fma as nvcc compiles it. */
+static float fused_element(const fused_src* s, int kv, int64_t token, int64_t kv_head, int64_t dim) {
+  const int64_t D = 128, channels = s->kv_heads * D, channel = kv_head * D + dim;
+  if (token < s->prefix_tokens) {
+    const uint8_t* st = s->bytestream + (kv ? s->value_offset : s->key_offset);
+    const int64_t sb = kv ? s->value_bytes : s->key_bytes;
+    if (s->codec == 0) {
+      if (token < s->sink_tokens) return h2f((kv ? s->value_sink : s->key_sink)[token * channels + channel]);
+      const int64_t body = s->prefix_tokens - s->sink_tokens, bt = token - s->sink_tokens;
+      if (!kv) {
+        const uint32_t sym = fused_symbol(st, sb, (dim * s->kv_heads + kv_head) * body + bt, s->bits);
+        const int64_t m = (bt / s->group_size) * channels + channel;
+        return fmaf((float)sym, h2f(s->key_scale[m]), h2f(s->key_zero[m]));
+      }
+      const int64_t groups = (channels + s->group_size - 1) / s->group_size;
+      const uint32_t sym = fused_symbol(st, sb, (kv_head * D + dim) * body + bt, s->bits);
+      const int64_t m = bt * groups + channel / s->group_size;
+      return fmaf((float)sym, h2f(s->value_scale[m]), h2f(s->value_zero[m]));
+    }
+    if (!kv) {
+      const uint32_t sym = fused_symbol(st, sb, (dim * s->kv_heads + kv_head) * s->prefix_tokens + token, s->bits);
+      return fmaf((float)sym, h2f(s->key_scale[channel]), h2f(s->key_zero[channel]));
+    }
+    const uint32_t sym = fused_symbol(st, sb, (kv_head * s->prefix_tokens + token) * D + dim, s->bits);
+    return fmaf((float)sym, h2f(s->value_scale[token]), h2f(s->value_zero[token]));
+  }
+  const int64_t pb = s->block_table[token / s->block_size];
+  if (pb < 0 || pb >= s->num_cache_blocks) return 0.f;
+  const int64_t off = token % s->block_size;
+  const int64_t i = s->blocks_first ? ((((pb * 2 + kv) * s->block_size + off) * s->kv_heads + kv_head) * D + dim)
+                                    : ((((kv * s->num_cache_blocks + pb) * s->block_size + off) * s->kv_heads + kv_head) * D + dim);
+  const uint16_t b = s->kv_cache[i];
+  return s->cache_bf16 ? bits_f32((uint32_t)b << 16) : h2f(b);
+}
+
+/* The reference kernel per (query token, query head): 4 warps score a 4-token tile (lane l
+ * sums dims l, l+32, l+64, l+96 with fma, then the shuffle-down tree folds the lanes), one
+ * thread updates the running max / sum with expf, and dim d accumulates
+ * acc * old_weight + sum_w weight_w * v_w. */
+void oracle_fused_prefix_attention(const uint8_t* bytestream, int64_t key_offset, int64_t key_bytes,
+                                   int64_t value_offset, int64_t value_bytes, int codec, int bits, int64_t group_size,
+                                   int64_t sink_tokens, const uint16_t* key_scale, const uint16_t* key_zero,
+                                   const uint16_t* value_scale, const uint16_t* value_zero, const uint16_t* key_sink,
+                                   const uint16_t* value_sink, const uint16_t* query, int query_bf16,
+                                   const uint16_t* kv_cache, int cache_bf16, int blocks_first, int64_t num_cache_blocks,
+                                   int64_t block_size, int64_t kv_heads, const int32_t* block_table,
+                                   int64_t prefix_tokens, int64_t query_start, int64_t sequence_length,
+                                   int64_t query_tokens, int64_t query_heads, float softmax_scale, uint16_t* output) {
+  const fused_src s = {bytestream, key_offset, key_bytes, value_offset, value_bytes, codec, bits, group_size,
+                       codec == 0 ? sink_tokens : 0, prefix_tokens, key_scale, key_zero, value_scale, value_zero,
+                       key_sink, value_sink, kv_cache, cache_bf16, blocks_first, num_cache_blocks, block_size,
+                       kv_heads, block_table};
+  const int64_t D = 128, group = query_heads / kv_heads;
+  const float NEG_INF = -__builtin_inff();
+#pragma omp parallel for collapse(2) schedule(dynamic)
+  for (int64_t qt = 0; qt < query_tokens; ++qt) {
+    for (int64_t qh = 0; qh < query_heads; ++qh) {
+      const int64_t kvh = qh / group;
+      int64_t causal_end = query_start + qt;
+      if (causal_end > sequence_length - 1) causal_end = sequence_length - 1;
+      float q[128], acc[128];
+      for (int64_t d = 0; d < D; ++d) {
+        const uint16_t b = query[(qt * query_heads + qh) * D + d];
+        q[d] = query_bf16 ? bits_f32((uint32_t)b << 16) : h2f(b);
+        acc[d] = 0.f;
+      }
+      float run_max = NEG_INF, run_sum = 0.f;
+      for (int64_t base = 0; base <= causal_end; base += 4) {
+        float scores[4], weights[4];
+        for (int w = 0; w < 4; ++w) {
+          const int64_t token = base + w;
+          if (token > causal_end) {
+            scores[w] = NEG_INF;
+            continue;
+          }
+          float lane[32];
+          for (int l = 0; l < 32; ++l) {
+            float dot = 0.f;
+            for (int64_t d = l; d < D; d += 32) dot = fmaf(q[d], fused_element(&s, 0, token, kvh, d), dot);
+            lane[l] = dot;
+          }
+          for (int off = 16; off > 0; off >>= 1) {
+            float next[32];
+            for (int l = 0; l < 32; ++l) next[l] = lane[l] + (l + off < 32 ? lane[l + off] : lane[l]);
+            memcpy(lane, next, sizeof(lane));
+          }
+          scores[w] = lane[0] * softmax_scale;
+        }
+        float tile_max = scores[0];
+        for (int w = 1; w < 4; ++w) tile_max = fmaxf(tile_max, scores[w]);
+        const float next_max = fmaxf(run_max, tile_max);
+        const float old_weight = expf(run_max - next_max);
+        float tile_sum = 0.f;
+        for (int w = 0; w < 4; ++w) {
+          weights[w] = base + w <= causal_end ? expf(scores[w] - next_max) : 0.f;
+          tile_sum += weights[w];
+        }
+        run_sum = fmaf(run_sum, old_weight, tile_sum);
+        run_max = next_max;
+        for (int64_t d = 0; d < D; ++d) {
+          float tile_acc = 0.f;
+          for (int w = 0; w < 4; ++w) {
+            const int64_t token = base + w;
+            if (token > causal_end) continue;
+            tile_acc = fmaf(weights[w], fused_element(&s, 1, token, kvh, d), tile_acc);
+          }
+          acc[d] = fmaf(acc[d], old_weight, tile_acc);
+        }
+      }
+      for (int64_t d = 0; d < D; ++d) output[(qt * query_heads + qh) * D + d] = out_at(acc[d] / run_sum, query_bf16);
+    }
+  }
+}

@@ -62,6 +62,9 @@ def lib():
         L.oracle_kivi_to_cache.restype = i64
         L.oracle_kivi_to_cache.argtypes = [vp, i64, i64, i64, i64, i64, i, i64, i64, vp, vp, vp, vp, vp, vp, i, vp, i,
                                            i, i64, vp, i64, i64, i64, i64, i64]
+        L.oracle_fused_prefix_attention.argtypes = [vp, i64, i64, i64, i64, i, i, i64, i64, vp, vp, vp, vp, vp, vp,
+                                                    vp, i, vp, i, i, i64, i64, i64, vp, i64, i64, i64, i64, i64,
+                                                    ctypes.c_float, vp]
         _lib = L
     return _lib
 
@@ -314,3 +317,28 @@ def kivi_to_cache(bytestream, key_offset, key_bytes, value_offset, value_bytes, 
         bs_.ctypes.data, len(bs_), key_offset, key_bytes, value_offset, value_bytes, bits, group_size, sink_tokens,
         *[m[0].ctypes.data for m in metas], half, cache.ctypes.data, int(out_is_bf16), int(blocks_first), nb,
         ids.ctypes.data, len(ids), bsz, tokens, H, D))
+
+
+def fused_prefix_attention(bytestream, key_offset, key_bytes, value_offset, value_bytes, codec, bits, group_size,
+                           sink_tokens, key_scale, key_zero, value_scale, value_zero, key_sink, value_sink,
+                           query: np.ndarray, query_bf16: bool, kv_cache: np.ndarray, cache_bf16: bool,
+                           blocks_first: bool, block_table, prefix_tokens: int, query_start: int, sequence_length: int,
+                           softmax_scale: float) -> np.ndarray:
+    """The reference fused prefix attention (cu:873-1091) on the CPU: query and kv_cache
+    hold fp16 / bf16 bit patterns (uint16), metadata is float16; returns the output bit
+    patterns, shaped like query."""
+    bs_ = np.ascontiguousarray(bytestream, dtype=np.uint8)
+    metas = [np.ascontiguousarray(m, dtype=np.float16) for m in (key_scale, key_zero, value_scale, value_zero,
+                                                                 key_sink, value_sink)]
+    q = np.ascontiguousarray(query, dtype=np.uint16)
+    cache = np.ascontiguousarray(kv_cache, dtype=np.uint16)
+    table = np.ascontiguousarray(block_table, dtype=np.int32)
+    nb, bsz, H, D = _cache_geom(cache, blocks_first)
+    assert D == 128 and q.ndim == 3 and q.shape[2] == 128
+    out = np.zeros_like(q)
+    lib().oracle_fused_prefix_attention(
+        bs_.ctypes.data, key_offset, key_bytes, value_offset, value_bytes, int(codec), int(bits), group_size,
+        sink_tokens, *[m.ctypes.data for m in metas], q.ctypes.data, int(query_bf16), cache.ctypes.data,
+        int(cache_bf16), int(blocks_first), nb, bsz, H, table.ctypes.data, prefix_tokens, query_start,
+        sequence_length, q.shape[0], q.shape[1], float(softmax_scale), out.ctypes.data)
+    return out

@@ -13,7 +13,7 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 CSRC = HERE / "csrc"
 LIB = HERE / "liborigami_b200.so"
-SOURCES = ["abi.cu", "quant.cu", "host_codec.cpp"]
+SOURCES = ["abi.cu", "quant.cu", "attention.cu", "host_codec.cpp"]
 # every kernel header and source, plus the public header
 DEPS = sorted(p.name for p in CSRC.iterdir() if p.suffix in (".cu", ".cuh", ".h", ".cpp")) + ["../../include/origami_b200.h"]
 
