@@ -22,6 +22,7 @@ from __future__ import annotations
 import argparse
 import datetime
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -46,10 +47,11 @@ def parse_args():
     ap.add_argument("--impl", choices=("origami", "reference"), default="origami")
     ap.add_argument("--planes", default="byte", help="byte | bit | bf16_bits | fp16_bits")
     ap.add_argument("--layers", type=int, default=0, help="layers (default: 32 for C2, 4 for C3, 8 for C5)")
-    ap.add_argument("--config", choices=("C2", "C3", "C5", "CG", "KIVI"), default="C2",
+    ap.add_argument("--config", choices=("C2", "C3", "C5", "CG", "KIVI", "ATTN"), default="C2",
                     help="workload (C2 is the headline; CG / KIVI: quantized restore paths)")
     ap.add_argument("--chunk-bytes", type=int, default=1 << 20, help="codec chunk size (min = target = max)")
     ap.add_argument("--tokens", type=int, default=0, help="C2 only: tokens per request (default 32768)")
+    ap.add_argument("--attn-queries", type=int, default=1, help="ATTN only: query tokens per step (default 1)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--bundle-e2e", action="store_true",
                     help="also restore from a bundle_v1 artifact through the host codec (codec-bound)")
@@ -1204,11 +1206,267 @@ def run_quant(args, rank, world, local, impl: str):
 
 
 
+# ----------------------------------------------------------------------------------------
+# compressed-prefix fused attention (--config ATTN)
+# ----------------------------------------------------------------------------------------
+# One decode step of a Llama-3-8B-shaped model over a C2-length request whose first 32768
+# tokens are a KIVI 2-bit prefix (kivi_adapter.py:138-145 defaults: group 64, 128 sink
+# tokens, fp16 metadata) and whose last `suffix` tokens sit in the paged bf16 cache; the
+# query is the newest token (32 query heads over 8 KV heads).
+ATTN = dict(layers=32, T=32768, suffix=256, H=8, QH=32, D=128, bs=16, bits=2, group_size=64, sink=128)
+
+
+class AttnWorkload:
+    """Per-layer KIVI prefix blobs (streams then fp16 metadata, 16-byte aligned parts),
+    paged caches holding the suffix, queries and outputs, all resident on the device."""
+
+    def __init__(self, layers: int, queries: int, device, seed: int = 11):
+        import torch
+
+        q = ATTN
+        self.layers, self.queries = layers, queries
+        T, H, D, bs, b, gs, sink = q["T"], q["H"], q["D"], q["bs"], q["bits"], q["group_size"], q["sink"]
+        C = H * D
+        self.T, self.H, self.QH, self.D, self.C = T, H, q["QH"], D, C
+        self.seq = T + q["suffix"]
+        self.q_start = self.seq - queries
+        body = T - sink
+        slen = (body * C * b + 7) // 8
+        kg, vg = (body + gs - 1) // gs, (C + gs - 1) // gs
+        self.slen = slen
+        parts = [("key", slen), ("value", slen), ("key_scale", 2 * kg * C), ("key_zero", 2 * kg * C),
+                 ("value_scale", 2 * body * vg), ("value_zero", 2 * body * vg), ("key_sink", 2 * sink * C),
+                 ("value_sink", 2 * sink * C)]
+        self.offsets, off = {}, 0
+        for name, n in parts:
+            off = (off + 15) // 16 * 16
+            self.offsets[name] = (off, n)
+            off += n
+        self.blob_bytes = off
+        self.prefix_bytes = sum(n for _, n in parts)
+        gd = torch.Generator(device=device).manual_seed(seed)
+        levels = (1 << b) - 1
+        self.blobs = []
+        for _ in range(layers):
+            blob = torch.zeros(self.blob_bytes, dtype=torch.uint8, device=device)
+            for name, n in parts:
+                o = self.offsets[name][0]
+                if name in ("key", "value"):
+                    blob[o:o + n] = torch.randint(0, 256, (n,), generator=gd, dtype=torch.uint8, device=device)
+                    continue
+                v = blob[o:o + n].view(torch.float16)
+                r = torch.rand(n // 2, generator=gd, device=device)
+                if name.endswith("scale"):
+                    v[:] = ((0.5 + r) * 2.0 / levels).half()
+                elif name.endswith("zero"):
+                    v[:] = (-1.2 + 0.4 * r).half()
+                else:
+                    v[:] = torch.randn(n // 2, generator=gd, device=device).half()
+            self.blobs.append(blob)
+        nb = (self.seq + bs - 1) // bs
+        self.NB = nb + 64
+        g = torch.Generator(device="cpu").manual_seed(seed)
+        self.table = torch.randperm(self.NB, generator=g)[:nb].to(torch.int32).to(device)
+        self.caches = [torch.randn((2, self.NB, bs, H, D), generator=gd, device=device).to(torch.bfloat16)
+                       for _ in range(layers)]
+        self.query = [torch.randn((queries, self.QH, D), generator=gd, device=device).to(torch.bfloat16)
+                      for _ in range(layers)]
+        self.out = [torch.empty_like(x) for x in self.query]
+        self.scale = 1.0 / math.sqrt(D)
+        # bytes one launch must read: the compressed prefix, the suffix K/V rows, the query
+        # (and write the output)
+        self.alg_bytes = self.prefix_bytes + 2 * q["suffix"] * C * 2 + 2 * queries * self.QH * D * 2
+        # bf16-equivalent K/V attended per step and layer
+        self.kv_equiv = 2 * self.seq * C * 2
+
+    def view(self, blob, name):
+        import torch
+
+        o, n = self.offsets[name]
+        return blob[o:o + n].view(torch.float16)
+
+    def args(self, layer: int, blob=None):
+        q = ATTN
+        blob = self.blobs[layer] if blob is None else blob
+        return [blob, self.offsets["key"][0], self.slen, self.offsets["value"][0], self.slen, 0, q["bits"],
+                q["group_size"], q["sink"], self.view(blob, "key_scale"), self.view(blob, "key_zero"),
+                self.view(blob, "value_scale"), self.view(blob, "value_zero"), self.view(blob, "key_sink"),
+                self.view(blob, "value_sink"), self.query[layer], self.caches[layer], self.table, self.T,
+                self.q_start, self.seq, self.scale, self.out[layer]]
+
+    def oracle_layer(self, layer: int) -> np.ndarray:
+        """The CPU oracle's output for one layer (checker; also the timed CPU sample)."""
+        sys.path.insert(0, str(REPO / "oracle"))
+        import oracle
+
+        q = ATTN
+        blob = self.blobs[layer].cpu().numpy()
+
+        def h(name):
+            o, n = self.offsets[name]
+            return blob[o:o + n].view(np.float16)
+
+        u16 = lambda t: t.view(__import__("torch").int16).cpu().numpy().view(np.uint16)  # noqa: E731
+        return oracle.fused_prefix_attention(
+            blob, self.offsets["key"][0], self.slen, self.offsets["value"][0], self.slen, 0, q["bits"],
+            q["group_size"], q["sink"], h("key_scale"), h("key_zero"), h("value_scale"), h("value_zero"),
+            h("key_sink"), h("value_sink"), u16(self.query[layer]), True, u16(self.caches[layer]), True, False,
+            self.table.cpu().numpy(), self.T, self.q_start, self.seq, self.scale)
+
+
+def _oracle_cores() -> int:
+    sys.path.insert(0, str(REPO / "oracle"))
+    import oracle
+
+    return oracle.max_threads()
+
+
+def run_attention(args, rank, world, local, impl: str):
+    """--config ATTN: the fused attention over a quantized prefix, one decode step over all
+    layers. `impl` origami times liborigami_b200.so (tcgen05 kernel); reference times the
+    reference's own kernel (csrc/origami/bitpack_layout_cuda.cu:873-1091) built from its
+    sources into oracle/_ref (rank 0 only)."""
+    import torch
+
+    if impl == "reference":
+        if rank != 0:
+            return 0
+        sys.path.insert(0, str(REPO / "tests" / "golden"))
+        from make_ref_vectors import load_reference_extension
+
+        ext = load_reference_extension()
+        if ext is None:
+            print(json.dumps({"impl": "reference", "unavailable": "reference extension not built in oracle/_ref "
+                              "(python oracle/build_ref.py needs the reference sources)"}), flush=True)
+            return 0
+        fn = ext.fused_prefix_attention_cuda
+        world_eff = 1
+    else:
+        from origami_b200 import attention
+
+        fn = attention.fused_prefix_attention_cuda
+        world_eff = world
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    layers = args.layers or ATTN["layers"]
+    wl = AttnWorkload(layers, args.attn_queries, device, seed=11 + rank)
+    stream = torch.cuda.current_stream(device)
+    kw = {}
+    flags = None
+    if impl == "origami":
+        from origami_b200 import attention
+
+        need = attention.workspace_bytes(wl.queries, wl.QH, wl.H, wl.q_start, wl.seq, device)
+        flags = torch.zeros(1, dtype=torch.int32, device=device)
+        kw = {"error_flags": flags}
+        if need:
+            kw["workspace"] = torch.zeros(need, dtype=torch.uint8, device=device)
+
+    def step(events=None):
+        for layer in range(layers):
+            if events is not None:
+                events.append((torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)))
+                events[-1][0].record(stream)
+            fn(*wl.args(layer), **kw)
+            if events is not None:
+                events[-1][1].record(stream)
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    ms, launch_ms = _graph_timed(step, args, world_eff, device)
+    clock_info = clocks.stop()
+    steps = args.steps
+    kv_gbs = wl.kv_equiv * layers * world_eff * steps / (ms / 1e3) / GB
+    peak, peak_kind = measured_hbm_peak()
+    mean_launch = sum(launch_ms) / len(launch_ms)
+    kernel = "prefix_attention" if impl == "origami" else "origami_fused_prefix_attention_kernel"
+    achieved = wl.alg_bytes / (mean_launch / 1e3) / GB
+    roof = {"kernel": kernel, "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind,
+            "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
+            "algorithmic_bytes_per_launch": wl.alg_bytes, "launch_ms": round(mean_launch, 5),
+            "us_per_layer": round(ms / steps / layers * 1e3, 2)}
+    q = ATTN
+    cfgd = {"workload": f"ATTN: Llama-3-8B decode step over a {q['T']}-token KIVI {q['bits']}-bit prefix "
+                        f"(group {q['group_size']}, {q['sink']} sink tokens) + {q['suffix']} paged bf16 tokens, "
+                        f"{wl.QH} query / {wl.H} KV heads, head_dim {q['D']}",
+            "layers": layers, "query_tokens": wl.queries, "requests": world_eff,
+            **{k: v for k, v in q.items() if k != "layers"}, "parallelism": f"replicas x{world_eff}, no collective",
+            "l2": f"inputs larger than L2 ({layers * wl.alg_bytes / 2**30:.2f} GiB read per rank per step)"}
+
+    ok = True
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        t0 = time.perf_counter()
+        want = wl.oracle_layer(0)
+        dt = time.perf_counter() - t0
+        got = wl.out[0].float().cpu().numpy()
+        ref = (want.astype(np.uint32) << 16).view(np.float32)
+        ok = bool(np.allclose(got, ref, atol=3e-2, rtol=3e-2))
+        cpu = {"value": round(wl.kv_equiv / dt / GB, 3), "unit": "GB/s", "cores": _oracle_cores(),
+               "kind": "port", "sample": f"1 layer ({wl.QH} query heads x {wl.seq} keys), oracle restatement of the "
+                                         f"reference kernel, {dt:.1f} s"}
+    if impl == "origami":
+        ok = ok and int(flags.item()) == 0
+
+    e2e = None
+    if impl == "origami" and not args.no_e2e:
+        host = [b.cpu().pin_memory() for b in wl.blobs]
+        dev = torch.empty_like(wl.blobs[0])
+        out_h = [torch.empty_like(o, device="cpu").pin_memory() for o in wl.out]
+
+        def e2e_step():
+            for layer in range(layers):
+                dev.copy_(host[layer], non_blocking=True)
+                fn(*wl.args(layer, blob=dev), **kw)
+                out_h[layer].copy_(wl.out[layer], non_blocking=True)
+
+        for _ in range(args.warmup):
+            e2e_step()
+        torch.cuda.synchronize(device)
+        barrier(world)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(steps):
+            e2e_step()
+        b.record(stream)
+        torch.cuda.synchronize(device)
+        ms_e2e = max_over_ranks(a.elapsed_time(b), world, device)
+        e2e = {"value": round(wl.kv_equiv * layers * world * steps / (ms_e2e / 1e3) / GB, 1), "unit": "GB/s",
+               "h2d_bytes_per_step": sum(int(h.numel()) for h in host),
+               "d2h_bytes_per_step": sum(int(o.numel()) * 2 for o in out_h), "ms_per_step": round(ms_e2e / steps, 3),
+               "note": "each layer's compressed prefix blob copied from pinned host, the fused attention, the output "
+                       "copied back"}
+
+    if rank == 0:
+        line = {"metric": "prefix attention: bf16-equivalent KV GB/s attended per decode step, whole job",
+                "value": round(kv_gbs, 1), "unit": "GB/s", "n_gpus": world_eff, "steps": steps,
+                "warmup": args.warmup, "ms_per_step": round(ms / steps, 4), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (fp32 dequant, fp32 accumulate)",
+                "data": "synthetic (seeded random symbol streams, metadata, suffix cache and queries)",
+                "config": cfgd, "roofline": roof, "gpu_launches": layers if impl == "origami" else 0,
+                "clocks": clock_info, "verified": ok}
+        if impl == "reference":
+            line["impl"] = "reference"
+            line["cpu_baseline"] = {"value": round(kv_gbs, 1), "unit": "GB/s", "cores": 0, "kind": "reference",
+                                    "sample": "the reference's CUDA kernel on the GPU (no CPU implementation exists)"}
+            line["e2e"] = {"value": round(kv_gbs, 1), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+        else:
+            if cpu is not None:
+                line["cpu_baseline"] = cpu
+            if e2e is not None:
+                line["e2e"] = e2e
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     args = parse_args()
     if args.config in QUANT:
         rank, world, local = init_dist("nccl")
         rc = run_quant(args, rank, world, local, args.impl)
+    elif args.config == "ATTN":
+        rank, world, local = init_dist("nccl")
+        rc = run_attention(args, rank, world, local, args.impl)
     elif args.impl == "reference":
         rank, world, _ = init_dist("gloo")
         rc = run_reference(args, rank, world)

@@ -294,6 +294,29 @@ int32_t origami_fused_prefix_attention_workspace(int64_t query_tokens, int64_t q
                                                  int64_t query_start_position, int64_t sequence_length,
                                                  int64_t* workspace_bytes);
 
+/* origami_fused_prefix_attention without a caller-provided workspace: the split
+ * workspace is a file-scope device array of 8 MiB per device inside the library, so the
+ * call allocates nothing. It serves hosts with no device allocator of their own (plain C
+ * or FFI bindings) and serving loops that must not call cudaMalloc, which can synchronise
+ * the whole device. No counterpart in the reference, whose kernel needs no workspace.
+ * - Shapes whose split plan needs more than 8 MiB are rejected (ORIGAMI_ERR_UNSUPPORTED,
+ *   message with both sizes); use the workspace entry point for those.
+ * - The first call on a device looks the array's address up (cudaGetSymbolAddress, with
+ *   that device current); make that first call before any stream capture.
+ * - Each call clears the arrival counters at the head of the array (cudaMemsetAsync on
+ *   `stream`) before the launch; nothing else has to start at zero.
+ * - All calls on a device share the one array: calls that overlap in time (other streams,
+ *   other threads) race and must be serialised by the caller. */
+int32_t origami_fused_prefix_attention_noalloc(
+    const uint8_t* d_bytestream, int64_t bytestream_bytes, int64_t key_offset, int64_t key_bytes,
+    int64_t value_offset, int64_t value_bytes, int64_t codec, int64_t bits, int64_t group_size, int64_t sink_tokens,
+    const void* d_key_scale, const void* d_key_zero, const void* d_value_scale, const void* d_value_zero,
+    const void* d_key_sink, const void* d_value_sink, const int64_t* meta_numel, int32_t meta_dtype,
+    const void* d_query, int32_t query_dtype, int64_t query_tokens, int64_t query_heads, int64_t head_dim,
+    const origami_paged_kv* cache, int32_t cache_dtype, const int32_t* d_block_table, int64_t block_table_len,
+    int64_t prefix_tokens, int64_t query_start_position, int64_t sequence_length, double softmax_scale,
+    void* d_output, uint32_t* d_error_flags, origami_stream_t stream);
+
 /* ---------------------------------------------------------------------------------
  * Host codec boundary (CPU only; no CUDA calls): the ORIGQZ1 chunk bundle and raw-deflate
  * chunk coding between caller-owned host buffers (pinned staging on the restore path)

@@ -110,6 +110,10 @@ def _declare(L: ctypes.CDLL) -> None:
     L.origami_fused_prefix_attention.restype = i32
     L.origami_fused_prefix_attention_workspace.argtypes = [i64, i64, i64, i64, i64, _vp]
     L.origami_fused_prefix_attention_workspace.restype = i32
+    L.origami_fused_prefix_attention_noalloc.argtypes = [
+        _vp, i64, i64, i64, i64, i64, i64, i64, i64, i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, i32, _vp, i32, i64, i64,
+        i64, P(PagedKV), i32, _vp, i64, i64, i64, i64, ctypes.c_double, _vp, _vp, _vp]
+    L.origami_fused_prefix_attention_noalloc.restype = i32
     L.origami_origqz1_parse.argtypes = [_vp, i64, _vp, i64, _vp, _vp, _vp, _vp]
     L.origami_origqz1_parse.restype = i32
     L.origami_deflate_bound.argtypes = [i64]
@@ -160,6 +164,7 @@ EXPORTS = (
     "origami_kivi_dequantize_to_kv_cache",
     "origami_fused_prefix_attention",
     "origami_fused_prefix_attention_workspace",
+    "origami_fused_prefix_attention_noalloc",
     "origami_origqz1_parse",
     "origami_deflate_bound",
     "origami_deflate_chunks",

@@ -255,3 +255,72 @@ int32_t origami_fused_prefix_attention(
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------
+// Allocation-free variant: the split workspace lives in a file-scope device array.
+// ---------------------------------------------------------------------------------------
+namespace {
+
+constexpr int64_t kStaticScratchBytes = 8ll << 20;  // 8 MiB per device
+__device__ __align__(256) uint8_t g_attention_scratch[kStaticScratchBytes];
+
+// The array's device address on the current device, looked up once per device.
+int32_t static_scratch(void** out) {
+  static std::mutex mu;
+  static std::vector<std::pair<int, void*>> cache;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  std::lock_guard<std::mutex> lock(mu);
+  for (const auto& x : cache)
+    if (x.first == dev) {
+      *out = x.second;
+      return ORIGAMI_OK;
+    }
+  void* p = nullptr;
+  if ((e = cudaGetSymbolAddress(&p, g_attention_scratch)) != cudaSuccess)
+    return cuda_fail(e, "cudaGetSymbolAddress(g_attention_scratch)");
+  cache.push_back({dev, p});
+  *out = p;
+  return ORIGAMI_OK;
+}
+
+}  // namespace
+
+extern "C" int32_t origami_fused_prefix_attention_noalloc(
+    const uint8_t* d_bytestream, int64_t bytestream_bytes, int64_t key_offset, int64_t key_bytes,
+    int64_t value_offset, int64_t value_bytes, int64_t codec, int64_t bits, int64_t group_size, int64_t sink_tokens,
+    const void* d_key_scale, const void* d_key_zero, const void* d_value_scale, const void* d_value_zero,
+    const void* d_key_sink, const void* d_value_sink, const int64_t* meta_numel, int32_t meta_dtype,
+    const void* d_query, int32_t query_dtype, int64_t query_tokens, int64_t query_heads, int64_t head_dim,
+    const origami_paged_kv* cache, int32_t cache_dtype, const int32_t* d_block_table, int64_t block_table_len,
+    int64_t prefix_tokens, int64_t query_start_position, int64_t sequence_length, double softmax_scale,
+    void* d_output, uint32_t* d_error_flags, origami_stream_t stream) {
+  if (cache == nullptr) return fail(ORIGAMI_ERR_INVALID, "kv cache is null");
+  int64_t need = 0;
+  int32_t rc = origami_fused_prefix_attention_workspace(query_tokens, query_heads, cache->num_heads,
+                                                        query_start_position, sequence_length, &need);
+  if (rc) return rc;
+  if (need > kStaticScratchBytes)
+    return fail(ORIGAMI_ERR_UNSUPPORTED,
+                "these shapes need %lld bytes of split workspace; the static scratch holds %lld "
+                "(use origami_fused_prefix_attention with a caller-provided workspace)",
+                static_cast<long long>(need), static_cast<long long>(kStaticScratchBytes));
+  void* scratch = nullptr;
+  if ((rc = static_scratch(&scratch))) return rc;
+  if (need > 0) {
+    // the arrival counters lead the workspace and must read zero at launch
+    AttnPlan p;
+    if ((rc = make_plan(query_tokens, query_heads, cache->num_heads, query_start_position, sequence_length, p)))
+      return rc;
+    const cudaError_t e =
+        cudaMemsetAsync(scratch, 0, static_cast<size_t>(p.counters_bytes), reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(scratch counters)");
+  }
+  return origami_fused_prefix_attention(
+      d_bytestream, bytestream_bytes, key_offset, key_bytes, value_offset, value_bytes, codec, bits, group_size,
+      sink_tokens, d_key_scale, d_key_zero, d_value_scale, d_value_zero, d_key_sink, d_value_sink, meta_numel,
+      meta_dtype, d_query, query_dtype, query_tokens, query_heads, head_dim, cache, cache_dtype, d_block_table,
+      block_table_len, prefix_tokens, query_start_position, sequence_length, softmax_scale, d_output, scratch,
+      kStaticScratchBytes, d_error_flags, stream);
+}
