@@ -61,7 +61,8 @@ int32_t make_plan(int64_t query_tokens, int64_t query_heads, int64_t kv_heads, i
   const int64_t base = kv_heads * p.row_blocks;
   const int64_t first_tiles = std::min(sequence_length - 1, query_start) / origami::attn::kKT + 1;
   int64_t splits = (2 * static_cast<int64_t>(sms) + base - 1) / base;
-  splits = std::max<int64_t>(1, std::min<int64_t>(splits, first_tiles));
+  // the merging CTA stages splits x NQ (max, sum) pairs in its 2 x 36 KB of tile memory
+  splits = std::max<int64_t>(1, std::min<int64_t>({splits, first_tiles, static_cast<int64_t>(4096 / p.nq)}));
   if (base * splits > 0x7FFFFFFF) return fail(ORIGAMI_ERR_UNSUPPORTED, "attention grid too large");
   p.splits = static_cast<int>(splits);
   if (p.splits > 1) {
@@ -239,6 +240,9 @@ int32_t origami_fused_prefix_attention(
   a.splits = p.splits;
   a.cache_bf16 = cache_dtype == ORIGAMI_DTYPE_BF16 ? 1 : 0;
   a.cache_vec = aligned(cache->d_data, 16) ? 1 : 0;
+  a.meta_vec = (aligned(d_key_scale, 16) && aligned(d_key_zero, 16) && aligned(d_value_scale, 16) &&
+                aligned(d_value_zero, 16)) ? 1 : 0;
+  a.sym_len = bits == 3 ? 3 : static_cast<int32_t>(bits);
   a.scale_log2 = static_cast<float>(softmax_scale * 1.4426950408889634);
   if (p.splits > 1) {
     uint8_t* ws = static_cast<uint8_t*>(d_workspace);

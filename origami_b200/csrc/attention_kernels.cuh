@@ -37,15 +37,15 @@ constexpr int kD = 128;            // head_dim
 constexpr int kKT = 128;           // keys per tile
 constexpr int kThreadsA = 256;
 constexpr int kLBO = 144;          // bytes between adjacent 8-element K chunks of a core-matrix row group
-constexpr int kSBO = 16 * kLBO;    // bytes between 8-row groups of a [rows x 128] operand tile
+constexpr int kSBO = 16 * kLBO + 16;  // bytes between 8-row groups of a [rows x 128] operand tile
 constexpr int kTileBytes = 16 * kSBO;  // a [128 x 128] 16-bit operand tile
 constexpr uint32_t kOCol = 64;     // TMEM column of O^T (S^T starts at column 0)
 constexpr uint32_t kTmemCols = 128;
 
 // Byte offset of element (row r, k) in a canonical [rows x 128] operand tile: 8 x 16-byte
-// core matrices, K chunks kLBO apart, row groups kSBO apart. The 16-byte padding per chunk
-// makes the dequant stores of 8 threads (8 chunks or 8 row groups apart) hit 8 different
-// bank quads.
+// core matrices, K chunks kLBO apart, row groups kSBO apart. The 16-byte paddings (kLBO =
+// 36 words, kSBO = 580 words, both 4 mod 32) make the 16-byte dequant stores of 8 threads
+// that are 8 chunks or 8 row groups apart hit 8 different bank quads.
 __device__ __forceinline__ uint32_t tile_off(int r, int k) {
   return static_cast<uint32_t>((r >> 3) * kSBO + (k >> 3) * kLBO + (r & 7) * 16 + (k & 7) * 2);
 }
@@ -182,6 +182,8 @@ struct AttnArgs {
   int64_t q_start, seq_len;
   int32_t q_tokens, q_heads, kv_heads, group, rows, row_blocks, splits;
   int32_t cache_bf16, cache_vec;  // cache element type; 16-byte aligned cache rows
+  int32_t meta_vec;               // scale / zero tensors 16-byte aligned (8-channel vector loads)
+  int32_t sym_len;                // bits per symbol value (3 for nibble-packed 3-bit)
   float scale_log2;               // softmax_scale * log2(e)
   float* ws_o;                    // [kv_heads * row_blocks * splits * NQ * 128] partial O
   float* ws_ml;                   // [kv_heads * row_blocks * splits * NQ * 2] partial max / sum
@@ -217,6 +219,91 @@ __device__ __forceinline__ uint64_t bits64(const AttnArgs& a, const uint8_t* s, 
 }
 
 __device__ __forceinline__ float h2f(const __half* p, int64_t i) { return __half2float(__ldg(p + i)); }
+
+// 32 or 64 stream bits from bit position `bit` as two words (bytes past the bytestream
+// read as 0); `narrow` (8 symbols of at most 4 bits) loads two aligned words instead of three.
+struct Win {
+  uint32_t lo, hi;
+};
+__device__ __forceinline__ Win window(const AttnArgs& a, const uint8_t* s, int64_t bit, bool narrow) {
+  const uintptr_t pa = reinterpret_cast<uintptr_t>(s + (bit >> 3));
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(pa & ~static_cast<uintptr_t>(3));
+  const uint32_t sh = static_cast<uint32_t>((pa & 3) * 8 + (bit & 7));
+  const uintptr_t end = (reinterpret_cast<uintptr_t>(a.bytes_end) + 3) & ~static_cast<uintptr_t>(3);
+  uint32_t w0, w1, w2 = 0u;
+  if (reinterpret_cast<uintptr_t>(w + 3) <= end) {
+    w0 = __ldg(w);
+    w1 = __ldg(w + 1);
+    if (!narrow) w2 = __ldg(w + 2);
+  } else {
+    uint32_t v[3] = {0u, 0u, 0u};
+    const uint8_t* b = reinterpret_cast<const uint8_t*>(w);
+    for (int i = 0; i < 12; ++i)
+      if (b + i < a.bytes_end) v[i >> 2] |= static_cast<uint32_t>(__ldg(b + i)) << ((i & 3) * 8);
+    w0 = v[0];
+    w1 = v[1];
+    w2 = v[2];
+  }
+  Win r;
+  r.lo = __funnelshift_r(w0, w1, sh);
+  r.hi = narrow ? 0u : __funnelshift_r(w1, w2, sh);
+  return r;
+}
+
+// The same without the end check, for windows known to end inside the bytestream.
+__device__ __forceinline__ Win window_in(const uint8_t* s, int64_t bit, bool narrow) {
+  const uintptr_t pa = reinterpret_cast<uintptr_t>(s + (bit >> 3));
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(pa & ~static_cast<uintptr_t>(3));
+  const uint32_t sh = static_cast<uint32_t>((pa & 3) * 8 + (bit & 7));
+  const uint32_t w0 = __ldg(w), w1 = __ldg(w + 1), w2 = narrow ? 0u : __ldg(w + 2);
+  Win r;
+  r.lo = __funnelshift_r(w0, w1, sh);
+  r.hi = narrow ? 0u : __funnelshift_r(w1, w2, sh);
+  return r;
+}
+// Whether the 12 bytes a window at `bit` may touch lie inside the bytestream's last word.
+__device__ __forceinline__ bool window_inside(const AttnArgs& a, const uint8_t* s, int64_t bit) {
+  const uintptr_t pa = reinterpret_cast<uintptr_t>(s + (bit >> 3)) & ~static_cast<uintptr_t>(3);
+  return pa + 12 <= ((reinterpret_cast<uintptr_t>(a.bytes_end) + 3) & ~static_cast<uintptr_t>(3));
+}
+
+// 8 windows at bit positions base + j * step (increasing), all loads issued before any use.
+__device__ __forceinline__ void windows8(const AttnArgs& a, const uint8_t* s, int64_t base, int64_t step, bool narrow,
+                                         Win (&w)[8]) {
+  if (window_inside(a, s, base + 7 * step)) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) w[j] = window_in(s, base + j * step, narrow);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) w[j] = window(a, s, base + j * step, narrow);
+  }
+}
+
+// The symbol at bit `pos` of a window as an exact float: bfe, then 2^23 + s - 2^23 (no
+// int -> float conversion instruction; exact for every symbol value).
+__device__ __forceinline__ float sym_at(const Win& w, uint32_t pos, uint32_t len) {
+  const uint32_t word = pos < 32 ? w.lo : w.hi;
+  uint32_t v;
+  asm("bfe.u32 %0, %1, %2, %3;" : "=r"(v) : "r"(word), "r"(pos & 31u), "r"(len));
+  return __uint_as_float(0x4B000000u | v) - 8388608.f;
+}
+
+// 8 consecutive fp16 values p[i .. i+7] as floats (one 16-byte load when `vec`).
+__device__ __forceinline__ void h2f8(const __half* p, int64_t i, bool vec, float (&o)[8]) {
+  if (vec) {
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(p + i));
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[k]));
+      o[2 * k] = f.x;
+      o[2 * k + 1] = f.y;
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) o[k] = h2f(p, i + k);
+  }
+}
 
 // Symbol `idx` of stream kv.
 __device__ __forceinline__ uint32_t symbol(const AttnArgs& a, int kv, int64_t idx) {
@@ -286,48 +373,117 @@ __device__ __forceinline__ void cache_row8(const AttnArgs& a, int kv, int64_t ke
   }
 }
 
+// 8 sink elements (dims 8*dq .. 8*dq + 7) of sink token `key` as 4 words of the query type.
+template <typename QT>
+__device__ __forceinline__ void sink_row8(const AttnArgs& a, int kv, int64_t key, int h, int dq, uint32_t (&w)[4]) {
+  const int64_t C = static_cast<int64_t>(a.kv_heads) * kD;
+  float f[8];
+  h2f8(a.sink_kv[kv], key * C + static_cast<int64_t>(h) * kD + 8 * dq, a.meta_vec != 0, f);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) w[i] = pack2<QT>(f[2 * i], f[2 * i + 1]);
+}
+
 }  // namespace attn
 
 namespace attn {
 
-// K block: keys kb .. kb+7 (rows) x dims 8*dq .. 8*dq+7, into the K tile at row group ko.
-// ksc / kze: per-dim key scale and zero (KVQuant only).
+// An 8 x 8 block element by element (sink tokens, octets that straddle the sink, prefix or
+// kmax boundaries): rows are keys (K) or dims (V^T). Rarely taken, so kept out of line
+// and not unrolled to keep the hot loop's code small.
 template <typename QT, int CODEC>
-__device__ __forceinline__ void k_block(const AttnArgs& a, int h, int64_t kb, int dq, int ko, int64_t kmax,
-                                        const float (&ksc)[8], const float (&kze)[8], uint8_t* tile) {
+__device__ __noinline__ void block_by_element(const AttnArgs& a, int kv, int h, int64_t kb, int dq, int64_t kmax,
+                                              uint8_t* dst) {
+  for (int r = 0; r < 8; ++r) {
+    uint32_t w4[4];
+    for (int w = 0; w < 4; ++w) {
+      const float lo = kv == 0 ? element<CODEC>(a, 0, kb + r, h, 8 * dq + 2 * w, kmax)
+                               : element<CODEC>(a, 1, kb + 2 * w, h, 8 * dq + r, kmax);
+      const float hi = kv == 0 ? element<CODEC>(a, 0, kb + r, h, 8 * dq + 2 * w + 1, kmax)
+                               : element<CODEC>(a, 1, kb + 2 * w + 1, h, 8 * dq + r, kmax);
+      w4[w] = pack2<QT>(lo, hi);
+    }
+    *reinterpret_cast<uint4*>(dst + r * 16) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+  }
+}
+
+// Per-thread constants of the dequant blocks (one CTA = one KV head h; the thread's K
+// block has dims 8*k_dq.., its V^T block dims 8*v_dq..).
+struct BlockCtx {
+  int64_t k_row0, k_row;  // K stream bit of (dim 8*k_dq, token 0); bits between consecutive dims
+  int64_t v_row0, v_row;  // V stream: KIVI (dim 8*v_dq, token 0) / dims; KVQuant (token 0, dim 8*v_dq) / tokens
+  int64_t v_cg0, v_cg7;   // KIVI value channel groups of dims 8*v_dq and 8*v_dq + 7
+  float ksc[8], kze[8];   // KVQuant per-channel key scale / zero of the K block's dims
+};
+
+template <int CODEC>
+__device__ __forceinline__ void block_ctx(const AttnArgs& a, int h, int k_dq, int v_dq, BlockCtx& c) {
+  const int64_t slot = a.slot_bits;
+  const int64_t run = CODEC == 0 ? a.body : a.prefix;  // tokens per K (and KIVI V) dim run
+  c.k_row0 = (static_cast<int64_t>(8 * k_dq) * a.kv_heads + h) * run * slot;
+  c.k_row = static_cast<int64_t>(a.kv_heads) * run * slot;
+  if (CODEC == 0) {
+    c.v_row0 = (static_cast<int64_t>(h) * kD + 8 * v_dq) * a.body * slot;
+    c.v_row = a.body * slot;
+    const int64_t ch0 = static_cast<int64_t>(h) * kD + 8 * v_dq;
+    c.v_cg0 = ch0 / a.group_size;
+    c.v_cg7 = (ch0 + 7) / a.group_size;
+  } else {
+    c.v_row0 = (static_cast<int64_t>(h) * a.prefix * kD + 8 * v_dq) * slot;
+    c.v_row = kD * slot;
+    c.v_cg0 = c.v_cg7 = 0;
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    c.ksc[j] = 0.f;
+    c.kze[j] = 0.f;
+  }
+  if (CODEC == 1) {
+    const int64_t ch0 = static_cast<int64_t>(h) * kD + 8 * k_dq;
+    h2f8(a.scale[0], ch0, a.meta_vec != 0, c.ksc);
+    h2f8(a.zero[0], ch0, a.meta_vec != 0, c.kze);
+  }
+}
+
+// K block: keys kb .. kb+7 (rows) x dims 8*dq .. 8*dq+7, into the K tile at row group ko.
+template <typename QT, int CODEC>
+__device__ __forceinline__ void k_block(const AttnArgs& a, const BlockCtx& c, int h, int64_t kb, int dq, int ko,
+                                        int64_t kmax, uint8_t* tile) {
   uint32_t m[8][4];
   const int64_t C = static_cast<int64_t>(a.kv_heads) * kD;
   const int64_t ch0 = static_cast<int64_t>(h) * kD + 8 * dq;
   const bool in_kmax = kb + 7 <= kmax;
   if (in_kmax && kb + 7 < a.prefix && (CODEC == 1 || kb >= a.sink)) {
-    // 8 consecutive symbols of each dim's run
+    // each dim's run holds the 8 keys consecutively
     const int64_t bt0 = CODEC == 0 ? kb - a.sink : kb;
-    const int64_t run = CODEC == 0 ? a.body : a.prefix;
-    uint64_t win[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j)
-      win[j] = bits64(a, a.stream[0], ((ch0 - static_cast<int64_t>(h) * kD + j) * a.kv_heads + h) * run * a.slot_bits +
-                                          bt0 * a.slot_bits);
+    const bool narrow = a.slot_bits <= 4;
+    const uint32_t slot = static_cast<uint32_t>(a.slot_bits), len = static_cast<uint32_t>(a.sym_len);
+    Win win[8];
+    windows8(a, a.stream[0], c.k_row0 + bt0 * a.slot_bits, c.k_row, narrow, win);
     float sc[8], ze[8];
-    int64_t g_prev = -1;
+    int64_t g = 0, r = 0;
+    if (CODEC == 0) {
+      g = bt0 / a.group_size;
+      r = bt0 - g * a.group_size;
+      h2f8(a.scale[0], g * C + ch0, a.meta_vec != 0, sc);
+      h2f8(a.zero[0], g * C + ch0, a.meta_vec != 0, ze);
+    }
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      if (CODEC == 0) {
-        const int64_t g = (bt0 + i) / a.group_size;
-        if (g != g_prev) {
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            sc[j] = h2f(a.scale[0], g * C + ch0 + j);
-            ze[j] = h2f(a.zero[0], g * C + ch0 + j);
-          }
-          g_prev = g;
+      if (CODEC == 0 && i > 0) {
+        // a group of at least 8 tokens changes at most once inside 8 keys
+        const int64_t gi = a.group_size >= 8 ? g + (r + i == a.group_size ? 1 : 0) : (bt0 + i) / a.group_size;
+        if (gi != g) {
+          g = gi;
+          if (a.group_size >= 8) r -= a.group_size;
+          h2f8(a.scale[0], g * C + ch0, a.meta_vec != 0, sc);
+          h2f8(a.zero[0], g * C + ch0, a.meta_vec != 0, ze);
         }
       }
       float v[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const float s = static_cast<float>(static_cast<uint32_t>(win[j] >> (i * a.slot_bits)) & a.sym_mask);
-        v[j] = CODEC == 0 ? __fmaf_rn(s, sc[j], ze[j]) : __fmaf_rn(s, ksc[j], kze[j]);
+        const float sy = sym_at(win[j], i * slot, len);
+        v[j] = CODEC == 0 ? __fmaf_rn(sy, sc[j], ze[j]) : __fmaf_rn(sy, c.ksc[j], c.kze[j]);
       }
 #pragma unroll
       for (int w = 0; w < 4; ++w) m[i][w] = pack2<QT>(v[2 * w], v[2 * w + 1]);
@@ -335,13 +491,12 @@ __device__ __forceinline__ void k_block(const AttnArgs& a, int h, int64_t kb, in
   } else if (in_kmax && kb >= a.prefix) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) cache_row8<QT>(a, 0, kb + i, h, dq, m[i]);
+  } else if (CODEC == 0 && in_kmax && kb + 7 < a.sink) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) sink_row8<QT>(a, 0, kb + i, h, dq, m[i]);
   } else {
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-#pragma unroll
-      for (int w = 0; w < 4; ++w)
-        m[i][w] = pack2<QT>(element<CODEC>(a, 0, kb + i, h, 8 * dq + 2 * w, kmax),
-                            element<CODEC>(a, 0, kb + i, h, 8 * dq + 2 * w + 1, kmax));
+    block_by_element<QT, CODEC>(a, 0, h, kb, dq, kmax, tile + ko * kSBO + dq * kLBO);
+    return;
   }
   uint8_t* dst = tile + ko * kSBO + dq * kLBO;
 #pragma unroll
@@ -350,40 +505,43 @@ __device__ __forceinline__ void k_block(const AttnArgs& a, int h, int64_t kb, in
 
 // V^T block: dims 8*dq .. 8*dq+7 (rows) x keys kb .. kb+7, into the V^T tile at row group dq.
 template <typename QT, int CODEC>
-__device__ __forceinline__ void v_block(const AttnArgs& a, int h, int64_t kb, int dq, int ko, int64_t kmax,
-                                        uint8_t* tile) {
+__device__ __forceinline__ void v_block(const AttnArgs& a, const BlockCtx& c, int h, int64_t kb, int dq, int ko,
+                                        int64_t kmax, uint8_t* tile) {
   uint32_t m[8][4];
   const int64_t C = static_cast<int64_t>(a.kv_heads) * kD;
   const int64_t ch0 = static_cast<int64_t>(h) * kD + 8 * dq;
   const bool in_kmax = kb + 7 <= kmax;
   if (in_kmax && kb + 7 < a.prefix && (CODEC == 1 || kb >= a.sink)) {
+    const bool narrow = a.slot_bits <= 4;
+    const uint32_t slot = static_cast<uint32_t>(a.slot_bits), len = static_cast<uint32_t>(a.sym_len);
     if (CODEC == 0) {
       // dim j's run holds the 8 keys consecutively; scale / zero by (key, channel group)
       const int64_t bt0 = kb - a.sink;
       const int64_t vg = (C + a.group_size - 1) / a.group_size;
-      const int64_t cg0 = ch0 / a.group_size, cg7 = (ch0 + 7) / a.group_size;
+      const bool one_group = c.v_cg0 == c.v_cg7;
+      Win wins[8];
+      windows8(a, a.stream[1], c.v_row0 + bt0 * a.slot_bits, c.v_row, narrow, wins);
       float sc[8], ze[8];
-      if (cg0 == cg7) {
+      if (one_group) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          sc[i] = h2f(a.scale[1], (bt0 + i) * vg + cg0);
-          ze[i] = h2f(a.zero[1], (bt0 + i) * vg + cg0);
+          sc[i] = h2f(a.scale[1], (bt0 + i) * vg + c.v_cg0);
+          ze[i] = h2f(a.zero[1], (bt0 + i) * vg + c.v_cg0);
         }
       }
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const uint64_t win = bits64(a, a.stream[1], ((ch0 + j) * a.body + bt0) * a.slot_bits);
+        const Win& win = wins[j];
         float v[8];
-        if (cg0 == cg7) {
+        if (one_group) {
 #pragma unroll
-          for (int i = 0; i < 8; ++i)
-            v[i] = __fmaf_rn(static_cast<float>(static_cast<uint32_t>(win >> (i * a.slot_bits)) & a.sym_mask), sc[i], ze[i]);
+          for (int i = 0; i < 8; ++i) v[i] = __fmaf_rn(sym_at(win, i * slot, len), sc[i], ze[i]);
         } else {
           const int64_t cg = (ch0 + j) / a.group_size;
 #pragma unroll
           for (int i = 0; i < 8; ++i)
-            v[i] = __fmaf_rn(static_cast<float>(static_cast<uint32_t>(win >> (i * a.slot_bits)) & a.sym_mask),
-                             h2f(a.scale[1], (bt0 + i) * vg + cg), h2f(a.zero[1], (bt0 + i) * vg + cg));
+            v[i] = __fmaf_rn(sym_at(win, i * slot, len), h2f(a.scale[1], (bt0 + i) * vg + cg),
+                             h2f(a.zero[1], (bt0 + i) * vg + cg));
         }
 #pragma unroll
         for (int w = 0; w < 4; ++w) m[j][w] = pack2<QT>(v[2 * w], v[2 * w + 1]);
@@ -391,14 +549,15 @@ __device__ __forceinline__ void v_block(const AttnArgs& a, int h, int64_t kb, in
     } else {
       // key i's run holds the 8 dims consecutively; one scale / zero per key. Rows are
       // built per key, then transposed to rows per dim.
+      Win wins[8];
+      windows8(a, a.stream[1], c.v_row0 + kb * c.v_row, c.v_row, narrow, wins);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const uint64_t win = bits64(a, a.stream[1], ((static_cast<int64_t>(h) * a.prefix + kb + i) * kD + 8 * dq) * a.slot_bits);
+        const Win& win = wins[i];
         const float sc = h2f(a.scale[1], kb + i), ze = h2f(a.zero[1], kb + i);
         float v[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-          v[j] = __fmaf_rn(static_cast<float>(static_cast<uint32_t>(win >> (j * a.slot_bits)) & a.sym_mask), sc, ze);
+        for (int j = 0; j < 8; ++j) v[j] = __fmaf_rn(sym_at(win, j * slot, len), sc, ze);
 #pragma unroll
         for (int w = 0; w < 4; ++w) m[i][w] = pack2<QT>(v[2 * w], v[2 * w + 1]);
       }
@@ -408,13 +567,13 @@ __device__ __forceinline__ void v_block(const AttnArgs& a, int h, int64_t kb, in
 #pragma unroll
     for (int i = 0; i < 8; ++i) cache_row8<QT>(a, 1, kb + i, h, dq, m[i]);
     transpose8x8_u16(m);
+  } else if (CODEC == 0 && in_kmax && kb + 7 < a.sink) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) sink_row8<QT>(a, 1, kb + i, h, dq, m[i]);
+    transpose8x8_u16(m);
   } else {
-#pragma unroll
-    for (int j = 0; j < 8; ++j)
-#pragma unroll
-      for (int w = 0; w < 4; ++w)
-        m[j][w] = pack2<QT>(element<CODEC>(a, 1, kb + 2 * w, h, 8 * dq + j, kmax),
-                            element<CODEC>(a, 1, kb + 2 * w + 1, h, 8 * dq + j, kmax));
+    block_by_element<QT, CODEC>(a, 1, h, kb, dq, kmax, tile + dq * kSBO + ko * kLBO);
+    return;
   }
   uint8_t* dst = tile + dq * kSBO + ko * kLBO;
 #pragma unroll
@@ -524,20 +683,11 @@ __global__ void __launch_bounds__(attn::kThreadsA, 2) prefix_attention(const __g
     l_run[tid] = 0.f;
     cend[tid] = row < a.rows ? min(a.seq_len - 1, a.q_start + row / a.group) : -1;
   }
-  // KVQuant key scale / zero of this thread's 8 K-block dims (constant over tiles)
-  const int k_dq = tid & 15, k_ko = tid >> 4;
+  // key octet fastest in both blocks: 16 lanes read one dim's run contiguously
+  const int k_ko = tid & 15, k_dq = tid >> 4;
   const int v_ko = tid & 15, v_dq = tid >> 4;
-  float ksc[8], kze[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    ksc[j] = 0.f;
-    kze[j] = 0.f;
-    if (CODEC == 1) {
-      const int64_t ch = static_cast<int64_t>(h) * kD + 8 * k_dq + j;
-      ksc[j] = h2f(a.scale[0], ch);
-      kze[j] = h2f(a.zero[0], ch);
-    }
-  }
+  BlockCtx bctx;
+  block_ctx<CODEC>(a, h, k_dq, v_dq, bctx);
   proxy_fence();
   tc_fence_before();
   __syncthreads();
@@ -551,7 +701,7 @@ __global__ void __launch_bounds__(attn::kThreadsA, 2) prefix_attention(const __g
     const int j = kt - t_begin;
     const int64_t k0 = static_cast<int64_t>(kt) * kKT;
     // K tile: its previous reader (MMA 1 of the previous tile) has completed.
-    k_block<QT, CODEC>(a, h, k0 + 8 * k_ko, k_dq, k_ko, kmax, ksc, kze, kt_sm);
+    k_block<QT, CODEC>(a, bctx, h, k0 + 8 * k_ko, k_dq, k_ko, kmax, kt_sm);
     if (j > 0) {  // V^T tile and P: wait for MMA 2 of the previous tile
       const bool ok = mbar_wait_bounded(&bars[1], ph2);
       ph2 ^= 1u;
@@ -560,7 +710,7 @@ __global__ void __launch_bounds__(attn::kThreadsA, 2) prefix_attention(const __g
         break;
       }
     }
-    v_block<QT, CODEC>(a, h, k0 + 8 * v_ko, v_dq, v_ko, kmax, vt_sm);
+    v_block<QT, CODEC>(a, bctx, h, k0 + 8 * v_ko, v_dq, v_ko, kmax, vt_sm);
     proxy_fence();
     tc_fence_before();
     __syncthreads();
@@ -702,24 +852,63 @@ __global__ void __launch_bounds__(attn::kThreadsA, 2) prefix_attention(const __g
       }
       __syncthreads();
       if (*last_flag) {
+        // Merge the splits: stage every split's (max, sum) in the free tile memory, turn them
+        // into per-row weights exp2(max_s - max) / sum once, then accumulate O with
+        // independent loads.
         __threadfence();
         const int64_t blk0 = (static_cast<int64_t>(h) * a.row_blocks + rb) * a.splits;
-        for (int e = tid; e < NQ * kD; e += kThreadsA) {
-          const int n = e / kD, d = e % kD;
-          const int row = row0 + n;
-          if (row >= a.rows) continue;
+        float* m_sm = reinterpret_cast<float*>(kt_sm);        // [splits][NQ]
+        float* w_sm = m_sm + static_cast<int64_t>(a.splits) * NQ;  // [splits][NQ]
+        for (int e = tid; e < a.splits * NQ; e += kThreadsA) {
+          m_sm[e] = __ldcg(a.ws_ml + (blk0 * NQ + e) * 2);
+          w_sm[e] = __ldcg(a.ws_ml + (blk0 * NQ + e) * 2 + 1);
+        }
+        __syncthreads();
+        if (tid < NQ) {
           float mx = -INFINITY;
-          for (int s2 = 0; s2 < a.splits; ++s2) mx = fmaxf(mx, __ldcg(a.ws_ml + ((blk0 + s2) * NQ + n) * 2));
-          float acc = 0.f, sum = 0.f;
+          for (int s2 = 0; s2 < a.splits; ++s2) mx = fmaxf(mx, m_sm[s2 * NQ + tid]);
+          float sum = 0.f;
           for (int s2 = 0; s2 < a.splits; ++s2) {
-            const float ms = __ldcg(a.ws_ml + ((blk0 + s2) * NQ + n) * 2);
+            const float ms = m_sm[s2 * NQ + tid];
             const float w = ms == -INFINITY ? 0.f : exp2f(ms - mx);
-            sum += w * __ldcg(a.ws_ml + ((blk0 + s2) * NQ + n) * 2 + 1);
-            acc += w * __ldcg(a.ws_o + ((blk0 + s2) * NQ + n) * kD + d);
+            sum += w * w_sm[s2 * NQ + tid];
+            m_sm[s2 * NQ + tid] = w;
           }
+          for (int s2 = 0; s2 < a.splits; ++s2) w_sm[s2 * NQ + tid] = m_sm[s2 * NQ + tid] / sum;
+        }
+        __syncthreads();
+        // NQ * 128 outputs, NQ / 2 per thread; up to 16 loads of a thread in flight
+        constexpr int kPer = NQ * kD / kThreadsA;
+        constexpr int kU = kPer >= 16 ? 1 : 16 / kPer;  // splits per round
+        float acc[kPer];
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) acc[k] = 0.f;
+        const float* o = a.ws_o + blk0 * NQ * kD;
+        int s2 = 0;
+        for (; s2 + kU <= a.splits; s2 += kU) {
+          float v[kPer][kU];
+#pragma unroll
+          for (int k = 0; k < kPer; ++k)
+#pragma unroll
+            for (int u = 0; u < kU; ++u) v[k][u] = __ldcg(o + static_cast<int64_t>(s2 + u) * NQ * kD + tid + k * kThreadsA);
+#pragma unroll
+          for (int k = 0; k < kPer; ++k)
+#pragma unroll
+            for (int u = 0; u < kU; ++u) acc[k] = __fmaf_rn(v[k][u], w_sm[(s2 + u) * NQ + (tid + k * kThreadsA) / kD], acc[k]);
+        }
+        for (; s2 < a.splits; ++s2)
+#pragma unroll
+          for (int k = 0; k < kPer; ++k)
+            acc[k] = __fmaf_rn(__ldcg(o + static_cast<int64_t>(s2) * NQ * kD + tid + k * kThreadsA),
+                               w_sm[s2 * NQ + (tid + k * kThreadsA) / kD], acc[k]);
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+          const int e = tid + k * kThreadsA;
+          const int row = row0 + e / kD, d = e % kD;
+          if (row >= a.rows) continue;
           const int64_t q = row / a.group;
           const int64_t qh = static_cast<int64_t>(h) * a.group + row % a.group;
-          a.output[(q * a.q_heads + qh) * kD + d] = from_float<QT>(acc / sum);
+          a.output[(q * a.q_heads + qh) * kD + d] = from_float<QT>(acc[k]);
         }
       }
     }
