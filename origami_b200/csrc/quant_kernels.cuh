@@ -354,6 +354,21 @@ __global__ void __launch_bounds__(kThreads) kivi_to_cache_elem(const __grid_cons
 // token octet is all sink or all body. UNI (group_size % 8 == 0): the value group of a
 // channel octet and the key group of a token octet are single groups.
 // Eight META values as one 16-byte-aligned vector access.
+// The four finished elements fma(s, scale, zero) for s = 0..3 as a table of two words
+// (entry s in bytes 2s, 2s + 1), so that symbols of at most 2 bits dequantize with one
+// byte permute instead of an int -> float and a float -> 16-bit conversion each.
+template <typename OUT>
+__device__ __forceinline__ uint2 lut4(float scale, float zero) {
+  return make_uint2(out_bits<OUT>(__fmaf_rn(0.f, scale, zero)) | (out_bits<OUT>(__fmaf_rn(1.f, scale, zero)) << 16),
+                    out_bits<OUT>(__fmaf_rn(2.f, scale, zero)) | (out_bits<OUT>(__fmaf_rn(3.f, scale, zero)) << 16));
+}
+// Two elements from one table: `pair` holds symbol s0 in byte 0 and s1 in byte 1.
+__device__ __forceinline__ uint32_t lut4_pair(uint2 t, uint32_t pair) {
+  return __byte_perm(t.x, t.y, 0x1010u + 0x22u * pair);
+}
+// One element (low 16 bits) from a table.
+__device__ __forceinline__ uint32_t lut4_one(uint2 t, uint32_t s) { return __byte_perm(t.x, t.y, 0x10u + 0x22u * s); }
+
 template <typename META>
 struct alignas(16) VecOf {
   META v[8];
@@ -530,16 +545,29 @@ __global__ void __launch_bounds__(kThreads) kivi_to_cache(const __grid_constant_
                 vz[i] = ze[idx];
               }
             }
+            if (bits <= 2) {
+              // one (scale, zero) per token row: a table per row, two channels per permute
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const float fs = to_f32(vs[i]);
-              const float fz = to_f32(vz[i]);
+              for (int i = 0; i < 8; ++i) {
+                const uint2 t = lut4<OUT>(to_f32(vs[i]), to_f32(vz[i]));
 #pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const uint32_t w = j < 2 ? lo[i] : hi[i];
-                const int sh = (j & 1) * 16;
-                outw[i][j] = out_bits<OUT>(__fmaf_rn(static_cast<float>((w >> sh) & 0xFF), fs, fz)) |
-                             (out_bits<OUT>(__fmaf_rn(static_cast<float>((w >> (sh + 8)) & 0xFF), fs, fz)) << 16);
+                for (int j = 0; j < 4; ++j) {
+                  const uint32_t w = j < 2 ? lo[i] : hi[i];
+                  outw[i][j] = lut4_pair(t, (w >> ((j & 1) * 16)) & 0x0303u);
+                }
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const float fs = to_f32(vs[i]);
+                const float fz = to_f32(vz[i]);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  const uint32_t w = j < 2 ? lo[i] : hi[i];
+                  const int sh = (j & 1) * 16;
+                  outw[i][j] = out_bits<OUT>(__fmaf_rn(static_cast<float>((w >> sh) & 0xFF), fs, fz)) |
+                               (out_bits<OUT>(__fmaf_rn(static_cast<float>((w >> (sh + 8)) & 0xFF), fs, fz)) << 16);
+                }
               }
             }
           } else {
@@ -559,17 +587,33 @@ __global__ void __launch_bounds__(kThreads) kivi_to_cache(const __grid_constant_
                 fz[j] = to_f32(ze[base + j]);
               }
             }
+            if (bits <= 2) {
+              // one (scale, zero) per channel: a table per channel, one permute per element
+              uint2 t[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
+              for (int j = 0; j < 8; ++j) t[j] = lut4<OUT>(fs[j], fz[j]);
 #pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const uint32_t w = j < 2 ? lo[i] : hi[i];
-                const int sh = (j & 1) * 16;
-                const int c = 2 * j;
-                outw[i][j] =
-                    out_bits<OUT>(__fmaf_rn(static_cast<float>((w >> sh) & 0xFF), fs[c], fz[c])) |
-                    (out_bits<OUT>(__fmaf_rn(static_cast<float>((w >> (sh + 8)) & 0xFF), fs[c + 1], fz[c + 1]))
-                     << 16);
+              for (int i = 0; i < 8; ++i) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  const uint32_t w = (j < 2 ? lo[i] : hi[i]) >> ((j & 1) * 16);
+                  outw[i][j] = __byte_perm(lut4_one(t[2 * j], w & 0x03u), lut4_one(t[2 * j + 1], (w >> 8) & 0x03u),
+                                           0x5410);
+                }
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  const uint32_t w = j < 2 ? lo[i] : hi[i];
+                  const int sh = (j & 1) * 16;
+                  const int c = 2 * j;
+                  outw[i][j] =
+                      out_bits<OUT>(__fmaf_rn(static_cast<float>((w >> sh) & 0xFF), fs[c], fz[c])) |
+                      (out_bits<OUT>(__fmaf_rn(static_cast<float>((w >> (sh + 8)) & 0xFF), fs[c + 1], fz[c + 1]))
+                       << 16);
+                }
               }
             }
           }
