@@ -108,6 +108,18 @@ def cases() -> list[dict]:
           query_tokens=9, query_start=160),
         c("kivi_b2_prefill_q40", 15, codec=0, bits=2, prefix=513, sink=16, group_size=64, kv_heads=2,
           query_heads=16, query_tokens=40, query_start=513),
+        # decode shapes whose groups fit the symbol-operand kernel: key groups of 64 / 96 / 128
+        # tokens (up to 3 per 128-key tile, boundaries off the tiles), value channel groups
+        # within a head, sinks off the 8-key octets
+        c("kivi_b2_g64_decode", 16, codec=0, bits=2, prefix=2000, sink=128, group_size=64, kv_heads=8,
+          query_heads=32, query_start=2099, seq_len=2100, query_bf16=True),
+        c("kivi_b4_g128_q4_ragged", 17, codec=0, bits=4, prefix=777, sink=5, group_size=128, kv_heads=2,
+          query_heads=8, query_tokens=4, query_start=800, seq_len=820),
+        c("kivi_b8_g64_blocks_first_mixed_bad", 18, codec=0, bits=8, prefix=300, sink=12, group_size=64,
+          kv_heads=4, query_heads=4, query_tokens=3, query_start=330, seq_len=360, blocks_first=True,
+          query_bf16=True, cache_bf16=False, bad_blocks=True),
+        c("kivi_b3_g96_q2", 19, codec=0, bits=3, prefix=500, sink=7, group_size=96, kv_heads=3, query_heads=6,
+          query_tokens=2, query_start=520, seq_len=540),
     ]
 
 
