@@ -10,6 +10,7 @@
 
 #include "../../include/origami_b200.h"
 #include "attention_kernels.cuh"
+#include "attention_sym_kernels.cuh"
 #include "host_common.h"
 
 using namespace origami_host;
@@ -48,12 +49,12 @@ int32_t sm_count(int& sms) {
 // Rows per CTA grow with the query rows of a KV head (8 .. 64); the key range is split
 // over CTAs until about two CTAs per SM are busy, at most one split per 128-key tile.
 int32_t make_plan(int64_t query_tokens, int64_t query_heads, int64_t kv_heads, int64_t query_start,
-                  int64_t sequence_length, AttnPlan& p) {
+                  int64_t sequence_length, bool sym, AttnPlan& p) {
   const int64_t group = query_heads / kv_heads;
   const int64_t rows = query_tokens * group;
   if (rows > 0x3FFFFFFF) return fail(ORIGAMI_ERR_UNSUPPORTED, "too many query rows");
   p.rows = static_cast<int>(rows);
-  p.nq = rows <= 8 ? 8 : rows <= 16 ? 16 : rows <= 32 ? 32 : 64;
+  p.nq = sym ? origami::attn::kSymNQ : rows <= 8 ? 8 : rows <= 16 ? 16 : rows <= 32 ? 32 : 64;
   p.row_blocks = static_cast<int>((rows + p.nq - 1) / p.nq);
   int sms = 0;
   const int32_t rc = sm_count(sms);
@@ -94,6 +95,47 @@ int32_t launch_nq(int nq, const origami::AttnArgs& a, int64_t ctas, cudaStream_t
   }
 }
 
+// The symbol-operand kernel (attention_sym_kernels.cuh) takes decode shapes (at most 32
+// query rows per KV head, 8 per CTA) whose groups fit its operand slots: KVQuant always,
+// KIVI when a 128-key tile spans at most 3 key groups and every head at most 2 value
+// channel groups.
+bool sym_path(int64_t codec, int64_t group_size, int64_t kv_heads, int64_t rows) {
+  if (rows > 4 * origami::attn::kSymNQ) return false;
+  if (codec == 1) return true;
+  if (group_size < 64) return false;
+  for (int64_t h = 0; h < kv_heads; ++h)
+    if ((h * 128 + 127) / group_size - (h * 128) / group_size + 1 > origami::attn::kSymMaxC) return false;
+  return true;
+}
+
+// Workspace for whichever kernel a call with these shapes takes: the larger plan.
+int32_t workspace_plan(int64_t query_tokens, int64_t query_heads, int64_t kv_heads, int64_t query_start,
+                       int64_t sequence_length, int64_t& bytes, int64_t& counters) {
+  AttnPlan p;
+  int32_t rc = make_plan(query_tokens, query_heads, kv_heads, query_start, sequence_length, false, p);
+  if (rc) return rc;
+  bytes = p.ws_bytes;
+  counters = p.counters_bytes;
+  if (query_tokens * (query_heads / kv_heads) <= 4 * origami::attn::kSymNQ) {
+    AttnPlan q;
+    if ((rc = make_plan(query_tokens, query_heads, kv_heads, query_start, sequence_length, true, q))) return rc;
+    bytes = std::max(bytes, q.ws_bytes);
+    counters = std::max(counters, q.counters_bytes);
+  }
+  return ORIGAMI_OK;
+}
+
+template <typename QT, int CODEC>
+int32_t launch_sym(const origami::AttnArgs& a, int64_t ctas, cudaStream_t st) {
+  const void* fn = reinterpret_cast<const void*>(&origami::prefix_attention_sym<QT, CODEC>);
+  const int smem = origami::AttnSymSmem::bytes(a.slot_bits);
+  int resident = 0;
+  int32_t rc = persistent_slots(fn, smem, resident);  // raises the kernel's shared-memory limit
+  if (rc) return rc;
+  origami::prefix_attention_sym<QT, CODEC><<<static_cast<unsigned>(ctas), origami::attn::kThreadsA, smem, st>>>(a);
+  return after_launch("prefix_attention_sym launch");
+}
+
 int64_t packed_symbol_bytes(int64_t bits, int64_t symbols) {
   return bits == 3 ? (symbols + 1) / 2 : (symbols * bits + 7) / 8;
 }
@@ -112,10 +154,11 @@ int32_t origami_fused_prefix_attention_workspace(int64_t query_tokens, int64_t q
     return fail(ORIGAMI_ERR_INVALID, "query_heads must be divisible by kv_heads");
   if (sequence_length <= 0 || query_start_position < 0 || query_start_position + query_tokens > sequence_length)
     return fail(ORIGAMI_ERR_INVALID, "query range exceeds sequence length");
-  AttnPlan p;
-  const int32_t rc = make_plan(query_tokens, query_heads, kv_heads, query_start_position, sequence_length, p);
+  int64_t bytes = 0, counters = 0;
+  const int32_t rc = workspace_plan(query_tokens, query_heads, kv_heads, query_start_position, sequence_length,
+                                    bytes, counters);
   if (rc) return rc;
-  *workspace_bytes = p.ws_bytes;
+  *workspace_bytes = bytes;
   return ORIGAMI_OK;
 }
 
@@ -196,8 +239,9 @@ int32_t origami_fused_prefix_attention(
   if (codec == 0 && sink_tokens > 0 && (d_key_sink == nullptr || d_value_sink == nullptr))
     return fail(ORIGAMI_ERR_INVALID, "KIVI sink tensors are too small");
 
+  const bool sym = sym_path(codec, group_size, kv_heads, query_tokens * (query_heads / kv_heads));
   AttnPlan p;
-  int32_t rc = make_plan(query_tokens, query_heads, kv_heads, query_start_position, sequence_length, p);
+  int32_t rc = make_plan(query_tokens, query_heads, kv_heads, query_start_position, sequence_length, sym, p);
   if (rc) return rc;
   if (p.ws_bytes > 0 && (d_workspace == nullptr || workspace_bytes < p.ws_bytes || !aligned(d_workspace, 16)))
     return fail(ORIGAMI_ERR_INVALID, "workspace must be 16-byte aligned and hold %lld bytes (zeroed before first use)",
@@ -207,6 +251,8 @@ int32_t origami_fused_prefix_attention(
   a.stream[0] = d_bytestream + key_offset;
   a.stream[1] = d_bytestream + value_offset;
   a.bytes_end = d_bytestream + bytestream_bytes;
+  a.stream_end[0] = a.stream[0] + key_bytes;
+  a.stream_end[1] = a.stream[1] + value_bytes;
   a.slot_bits = bits == 3 ? 4 : static_cast<int32_t>(bits);
   a.sym_mask = static_cast<int32_t>((1 << bits) - 1);
   a.group_size = group_size;
@@ -253,6 +299,11 @@ int32_t origami_fused_prefix_attention(
   a.err = d_error_flags;
   const int64_t ctas = kv_heads * p.row_blocks * p.splits;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (sym) {
+    if (query_dtype == ORIGAMI_DTYPE_BF16)
+      return codec == 0 ? launch_sym<__nv_bfloat16, 0>(a, ctas, st) : launch_sym<__nv_bfloat16, 1>(a, ctas, st);
+    return codec == 0 ? launch_sym<__half, 0>(a, ctas, st) : launch_sym<__half, 1>(a, ctas, st);
+  }
   if (query_dtype == ORIGAMI_DTYPE_BF16)
     return codec == 0 ? launch_nq<__nv_bfloat16, 0>(p.nq, a, ctas, st) : launch_nq<__nv_bfloat16, 1>(p.nq, a, ctas, st);
   return codec == 0 ? launch_nq<__half, 0>(p.nq, a, ctas, st) : launch_nq<__half, 1>(p.nq, a, ctas, st);
@@ -314,11 +365,12 @@ extern "C" int32_t origami_fused_prefix_attention_noalloc(
   if ((rc = static_scratch(&scratch))) return rc;
   if (need > 0) {
     // the arrival counters lead the workspace and must read zero at launch
-    AttnPlan p;
-    if ((rc = make_plan(query_tokens, query_heads, cache->num_heads, query_start_position, sequence_length, p)))
+    int64_t bytes = 0, counters = 0;
+    if ((rc = workspace_plan(query_tokens, query_heads, cache->num_heads, query_start_position, sequence_length,
+                             bytes, counters)))
       return rc;
     const cudaError_t e =
-        cudaMemsetAsync(scratch, 0, static_cast<size_t>(p.counters_bytes), reinterpret_cast<cudaStream_t>(stream));
+        cudaMemsetAsync(scratch, 0, static_cast<size_t>(counters), reinterpret_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(scratch counters)");
   }
   return origami_fused_prefix_attention(

@@ -168,6 +168,7 @@ __device__ __forceinline__ void transpose8x8_u16(uint32_t (&m)[8][4]) {
 struct AttnArgs {
   const uint8_t* stream[2];      // key / value symbol streams (bytestream + offset)
   const uint8_t* bytes_end;      // end of the bytestream: no load reaches past its 4-byte word
+  const uint8_t* stream_end[2];  // ends of the key / value streams (stream + key_bytes / value_bytes)
   int32_t slot_bits, sym_mask;   // bits per symbol slot (4 for nibble-packed 3-bit) and value mask
   int64_t group_size, sink, prefix, body;  // body = tokens held in the symbol streams
   const __half* scale[2];        // KIVI: key [ceil(body/gs), C], value [body, ceil(C/gs)]; KVQuant: key [C], value [prefix]
@@ -610,6 +611,81 @@ __device__ __forceinline__ void named_sync_softmax() { asm volatile("bar.sync 1,
 
 }  // namespace attn
 
+// Merge of the splits of one row block by the CTA that finished last. One warp per row
+// turns the splits' (max, sum) into weights exp2(max_s - max) / sum in `stage` (splits * NQ
+// floats of free shared memory); then each thread accumulates NQ / 8 float4 of O over the
+// splits, 8 float4 loads in flight.
+template <typename QT, int NQ>
+__device__ __forceinline__ void split_merge(const AttnArgs& a, int h, int rb, int row0, float* stage) {
+  using namespace attn;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  __threadfence();
+  const int64_t blk0 = (static_cast<int64_t>(h) * a.row_blocks + rb) * a.splits;
+  float* w_sm = stage;  // [splits][NQ]
+  for (int n = warp; n < NQ; n += kThreadsA / 32) {
+    float mx = -INFINITY;
+    for (int s2 = lane; s2 < a.splits; s2 += 32) mx = fmaxf(mx, __ldcg(a.ws_ml + ((blk0 + s2) * NQ + n) * 2));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float sum = 0.f;
+    for (int s2 = lane; s2 < a.splits; s2 += 32) {
+      const float ms = __ldcg(a.ws_ml + ((blk0 + s2) * NQ + n) * 2);
+      const float w = ms == -INFINITY ? 0.f : exp2f(ms - mx);
+      sum += w * __ldcg(a.ws_ml + ((blk0 + s2) * NQ + n) * 2 + 1);
+      w_sm[s2 * NQ + n] = w;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    const float inv = 1.f / sum;
+    __syncwarp();
+    for (int s2 = lane; s2 < a.splits; s2 += 32) w_sm[s2 * NQ + n] *= inv;
+  }
+  __syncthreads();
+  constexpr int kPer = NQ * kD / 4 / kThreadsA;  // float4 of O per thread
+  constexpr int kU = kPer >= 8 ? 1 : 8 / kPer;   // splits per round
+  float4 acc[kPer];
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+  const float4* o = reinterpret_cast<const float4*>(a.ws_o + blk0 * NQ * kD);
+  constexpr int kSplit4 = NQ * kD / 4;  // float4 per split
+  int s2 = 0;
+  auto fma4 = [](float4& c, const float4& v, float w) {
+    c.x = __fmaf_rn(v.x, w, c.x);
+    c.y = __fmaf_rn(v.y, w, c.y);
+    c.z = __fmaf_rn(v.z, w, c.z);
+    c.w = __fmaf_rn(v.w, w, c.w);
+  };
+  for (; s2 + kU <= a.splits; s2 += kU) {
+    float4 v[kPer][kU];
+#pragma unroll
+    for (int k = 0; k < kPer; ++k)
+#pragma unroll
+      for (int u = 0; u < kU; ++u) v[k][u] = __ldcg(o + static_cast<int64_t>(s2 + u) * kSplit4 + tid + k * kThreadsA);
+#pragma unroll
+    for (int k = 0; k < kPer; ++k)
+#pragma unroll
+      for (int u = 0; u < kU; ++u) fma4(acc[k], v[k][u], w_sm[(s2 + u) * NQ + (tid + k * kThreadsA) / (kD / 4)]);
+  }
+  for (; s2 < a.splits; ++s2)
+#pragma unroll
+    for (int k = 0; k < kPer; ++k)
+      fma4(acc[k], __ldcg(o + static_cast<int64_t>(s2) * kSplit4 + tid + k * kThreadsA),
+           w_sm[s2 * NQ + (tid + k * kThreadsA) / (kD / 4)]);
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    const int f = tid + k * kThreadsA;
+    const int row = row0 + f / (kD / 4), d = (f % (kD / 4)) * 4;
+    if (row >= a.rows) continue;
+    const int64_t q = row / a.group;
+    const int64_t qh = static_cast<int64_t>(h) * a.group + row % a.group;
+    uint16_t* out = a.output + (q * a.q_heads + qh) * kD + d;
+    out[0] = from_float<QT>(acc[k].x);
+    out[1] = from_float<QT>(acc[k].y);
+    out[2] = from_float<QT>(acc[k].z);
+    out[3] = from_float<QT>(acc[k].w);
+  }
+}
+
 template <int NQ>
 struct AttnSmem {
   static constexpr int q_bytes = (NQ / 8) * attn::kSBO;  // Q rows and P rows, [NQ x 128] each
@@ -852,64 +928,7 @@ __global__ void __launch_bounds__(attn::kThreadsA, 2) prefix_attention(const __g
       }
       __syncthreads();
       if (*last_flag) {
-        // Merge the splits: stage every split's (max, sum) in the free tile memory, turn them
-        // into per-row weights exp2(max_s - max) / sum once, then accumulate O with
-        // independent loads.
-        __threadfence();
-        const int64_t blk0 = (static_cast<int64_t>(h) * a.row_blocks + rb) * a.splits;
-        float* m_sm = reinterpret_cast<float*>(kt_sm);        // [splits][NQ]
-        float* w_sm = m_sm + static_cast<int64_t>(a.splits) * NQ;  // [splits][NQ]
-        for (int e = tid; e < a.splits * NQ; e += kThreadsA) {
-          m_sm[e] = __ldcg(a.ws_ml + (blk0 * NQ + e) * 2);
-          w_sm[e] = __ldcg(a.ws_ml + (blk0 * NQ + e) * 2 + 1);
-        }
-        __syncthreads();
-        if (tid < NQ) {
-          float mx = -INFINITY;
-          for (int s2 = 0; s2 < a.splits; ++s2) mx = fmaxf(mx, m_sm[s2 * NQ + tid]);
-          float sum = 0.f;
-          for (int s2 = 0; s2 < a.splits; ++s2) {
-            const float ms = m_sm[s2 * NQ + tid];
-            const float w = ms == -INFINITY ? 0.f : exp2f(ms - mx);
-            sum += w * w_sm[s2 * NQ + tid];
-            m_sm[s2 * NQ + tid] = w;
-          }
-          for (int s2 = 0; s2 < a.splits; ++s2) w_sm[s2 * NQ + tid] = m_sm[s2 * NQ + tid] / sum;
-        }
-        __syncthreads();
-        // NQ * 128 outputs, NQ / 2 per thread; up to 16 loads of a thread in flight
-        constexpr int kPer = NQ * kD / kThreadsA;
-        constexpr int kU = kPer >= 16 ? 1 : 16 / kPer;  // splits per round
-        float acc[kPer];
-#pragma unroll
-        for (int k = 0; k < kPer; ++k) acc[k] = 0.f;
-        const float* o = a.ws_o + blk0 * NQ * kD;
-        int s2 = 0;
-        for (; s2 + kU <= a.splits; s2 += kU) {
-          float v[kPer][kU];
-#pragma unroll
-          for (int k = 0; k < kPer; ++k)
-#pragma unroll
-            for (int u = 0; u < kU; ++u) v[k][u] = __ldcg(o + static_cast<int64_t>(s2 + u) * NQ * kD + tid + k * kThreadsA);
-#pragma unroll
-          for (int k = 0; k < kPer; ++k)
-#pragma unroll
-            for (int u = 0; u < kU; ++u) acc[k] = __fmaf_rn(v[k][u], w_sm[(s2 + u) * NQ + (tid + k * kThreadsA) / kD], acc[k]);
-        }
-        for (; s2 < a.splits; ++s2)
-#pragma unroll
-          for (int k = 0; k < kPer; ++k)
-            acc[k] = __fmaf_rn(__ldcg(o + static_cast<int64_t>(s2) * NQ * kD + tid + k * kThreadsA),
-                               w_sm[s2 * NQ + (tid + k * kThreadsA) / kD], acc[k]);
-#pragma unroll
-        for (int k = 0; k < kPer; ++k) {
-          const int e = tid + k * kThreadsA;
-          const int row = row0 + e / kD, d = e % kD;
-          if (row >= a.rows) continue;
-          const int64_t q = row / a.group;
-          const int64_t qh = static_cast<int64_t>(h) * a.group + row % a.group;
-          a.output[(q * a.q_heads + qh) * kD + d] = from_float<QT>(acc[k]);
-        }
+        split_merge<QT, NQ>(a, h, rb, row0, reinterpret_cast<float*>(kt_sm));
       }
     }
   }
