@@ -53,7 +53,7 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 // Element (kv, key, dim d of head h) as the symbol tiles hold it: the raw symbol for a
 // body key, the value for sink / suffix keys, 0 past kmax.
 template <int CODEC>
-__device__ float element_sym(const AttnArgs& a, int kv, int64_t key, int h, int d, int64_t kmax) {
+__device__ float element_sym(const AttnArgs& a, int kv, int64_t key, int h, int d, int64_t kmax, float bias) {
   if (key > kmax) return 0.f;
   if (key < a.prefix && (CODEC == 1 || key >= a.sink)) {
     const int64_t bt = CODEC == 0 ? key - a.sink : key;
@@ -61,7 +61,7 @@ __device__ float element_sym(const AttnArgs& a, int kv, int64_t key, int h, int 
     if (kv == 0) idx = (static_cast<int64_t>(d) * a.kv_heads + h) * a.body + bt;
     else if (CODEC == 0) idx = (static_cast<int64_t>(h) * kD + d) * a.body + bt;
     else idx = (static_cast<int64_t>(h) * a.prefix + key) * kD + d;
-    return static_cast<float>(symbol(a, kv, idx));
+    return bias + static_cast<float>(symbol(a, kv, idx));
   }
   return element<CODEC>(a, kv, key, h, d, kmax);
 }
@@ -96,6 +96,64 @@ __device__ __forceinline__ uint4 sym8(const uint2* lut, const Win& w, int slot) 
   return make_uint4(v[0], v[1], v[2], v[3]);
 }
 
+// 8 consecutive symbols of a window (low symbol first) as 4 words of 16-bit values
+// bias + s, built with byte permutes: the bit pattern 0x4300 | s is 128 + s in bf16,
+// 0x6400 | s is 1024 + s in fp16 (s below 128 / 1024: exact). bf16 with 8-bit symbols
+// (s up to 255) goes through the byte table instead, with bias 0.
+template <int SLOT, bool BF16>
+__device__ __forceinline__ uint4 sym8_bias(const Win& w, const uint2* lut, uint32_t mask4) {
+  if constexpr (SLOT == 2) {
+    constexpr uint32_t C = BF16 ? 0x43004300u : 0x64006400u;
+    const uint32_t m = w.lo & 0x3333u, e = (w.lo >> 2) & 0x3333u;  // even / odd symbols, 2 per byte
+    const uint32_t t01 = __byte_perm(m, e, 0x4400), t23 = __byte_perm(m, e, 0x5511);
+    return make_uint4((t01 & 0x00030003u) | C, ((t01 >> 4) & 0x00030003u) | C, (t23 & 0x00030003u) | C,
+                      ((t23 >> 4) & 0x00030003u) | C);
+  } else if constexpr (SLOT == 4) {
+    constexpr uint32_t CR = BF16 ? 0x43434343u : 0x64646464u;
+    const uint32_t y = w.lo & mask4, z = (w.lo >> 4) & mask4;  // even / odd symbols, 1 per byte
+    const uint32_t t = __byte_perm(y, z, 0x5140), u = __byte_perm(y, z, 0x7362);
+    return make_uint4(__byte_perm(t, CR, 0x4140), __byte_perm(t, CR, 0x4342), __byte_perm(u, CR, 0x4140),
+                      __byte_perm(u, CR, 0x4342));
+  } else {
+    if constexpr (BF16) return sym8(lut, w, 8);
+    constexpr uint32_t CR = 0x64646464u;
+    return make_uint4(__byte_perm(w.lo, CR, 0x4140), __byte_perm(w.lo, CR, 0x4342), __byte_perm(w.hi, CR, 0x4140),
+                      __byte_perm(w.hi, CR, 0x4342));
+  }
+}
+template <bool BF16>
+__host__ __device__ constexpr float sym_bias(int slot) {
+  return BF16 ? (slot == 8 ? 0.f : 128.f) : 1024.f;
+}
+
+// 64 symbols of a staged run from bit `sh` of src[0] (8 octets; octet o goes to
+// dst + o * stride when bit o of `octets` is set).
+template <int SLOT, bool BF16>
+__device__ __forceinline__ void decode_half_run(const uint32_t* src, uint32_t sh, uint32_t octets, uint8_t* dst,
+                                                int stride, const uint2* lut, uint32_t mask4) {
+  constexpr int NW = 2 * SLOT;
+  uint32_t raw[NW + 1], n[NW];
+#pragma unroll
+  for (int i = 0; i <= NW; ++i) raw[i] = src[i];
+#pragma unroll
+  for (int i = 0; i < NW; ++i) n[i] = __funnelshift_r(raw[i], raw[i + 1], sh);
+#pragma unroll
+  for (int o = 0; o < 8; ++o) {
+    if (!((octets >> o) & 1u)) continue;
+    Win w;
+    w.hi = 0u;
+    if constexpr (SLOT == 2) {
+      w.lo = n[o >> 1] >> (16 * (o & 1));
+    } else if constexpr (SLOT == 4) {
+      w.lo = n[o];
+    } else {
+      w.lo = n[2 * o];
+      w.hi = n[2 * o + 1];
+    }
+    *reinterpret_cast<uint4*>(dst + o * stride) = sym8_bias<SLOT, BF16>(w, lut, mask4);
+  }
+}
+
 // The 8 symbols at bit `pos` of a staged run (`pos` counted from the run's first word).
 __device__ __forceinline__ Win staged_window(const uint32_t* run, uint32_t pos, bool narrow) {
   const uint32_t* w = run + (pos >> 5);
@@ -106,18 +164,12 @@ __device__ __forceinline__ Win staged_window(const uint32_t* run, uint32_t pos, 
   return r;
 }
 
-// Octet of 8 keys kb .. kb+7: all body keys of the prefix (symbols), or not.
-template <int CODEC>
-__device__ __forceinline__ bool body_octet(const AttnArgs& a, int64_t kb, int64_t kmax) {
-  return kb + 7 <= kmax && kb + 7 < a.prefix && (CODEC == 1 || kb >= a.sink);
-}
-
 // 8 x 8 block of keys kb.. x dims 8*dq.. in a non-body octet, as rows per key (real
-// values for sink / suffix keys, raw symbols for body keys, element by element at mixed
+// values for sink / suffix keys, bias + symbol for body keys, element by element at mixed
 // octets).
 template <typename QT, int CODEC>
 __device__ __forceinline__ void real_rows8(const AttnArgs& a, int kv, int h, int64_t kb, int dq, int64_t kmax,
-                                           uint32_t (&m)[8][4]) {
+                                           float bias, uint32_t (&m)[8][4]) {
   if (kb + 7 <= kmax && kb >= a.prefix) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) cache_row8<QT>(a, kv, kb + i, h, dq, m[i]);
@@ -129,8 +181,8 @@ __device__ __forceinline__ void real_rows8(const AttnArgs& a, int kv, int h, int
     for (int i = 0; i < 8; ++i)
 #pragma unroll
       for (int w = 0; w < 4; ++w)
-        m[i][w] = pack2<QT>(element_sym<CODEC>(a, kv, kb + i, h, 8 * dq + 2 * w, kmax),
-                            element_sym<CODEC>(a, kv, kb + i, h, 8 * dq + 2 * w + 1, kmax));
+        m[i][w] = pack2<QT>(element_sym<CODEC>(a, kv, kb + i, h, 8 * dq + 2 * w, kmax, bias),
+                            element_sym<CODEC>(a, kv, kb + i, h, 8 * dq + 2 * w + 1, kmax, bias));
   }
 }
 
@@ -142,6 +194,31 @@ __device__ __forceinline__ uint4 load8h(const __half* p, int64_t i, bool vec) {
 #pragma unroll
   for (int k = 0; k < 4; ++k) w[k] = static_cast<uint32_t>(__ldg(q + 2 * k)) | (static_cast<uint32_t>(__ldg(q + 2 * k + 1)) << 16);
   return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// KVQuant V^T tile (MN-major: dims contiguous per key) from the head's staged symbols:
+// dim octet u_lo of keys u_hi + 16 r, body octets [ob_lo, ob_hi) only.
+template <int SLOT, bool BF16>
+__device__ __forceinline__ void decode_kvq_v(const uint32_t* rawv, uint32_t sh0, int u_lo, int u_hi, int ob_lo,
+                                             int ob_hi, uint8_t* vt_sm, const uint2* lut, uint32_t mask4) {
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    const int tl = u_hi + 16 * r;
+    if ((tl >> 3) < ob_lo || (tl >> 3) >= ob_hi) continue;
+    const Win w = staged_window(rawv, sh0 + static_cast<uint32_t>((tl * kD + 8 * u_lo) * SLOT), SLOT != 8);
+    *reinterpret_cast<uint4*>(vt_sm + u_lo * kSBO + (tl >> 3) * kLBO + (tl & 7) * 16) = sym8_bias<SLOT, BF16>(w, lut, mask4);
+  }
+}
+
+// Barrier 1 over warps 0..3 (the softmax warps) with an OR vote.
+__device__ __forceinline__ bool named_sync_or_softmax(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 q, %1, 0;\n barrier.cta.red.or.pred p, 1, 128, q;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v))
+      : "memory");
+  return r != 0u;
 }
 
 // Key range, body range and key groups of tile kt.
@@ -180,10 +257,11 @@ struct AttnSymSmem {
   static constexpr int bq_off = lut_off + 256 * 8;                             // [32 x 128]: q (.) scale_g, q
   static constexpr int ps_off = bq_off + (attn::kSymMaxG + 1) * attn::kRowTile;  // [16 x 128]: P (.) vscale_c
   static constexpr int f_off = ps_off + attn::kSymMaxC * attn::kRowTile;
-  // floats: red[4][8], redz[2][4][8], m_run, l_run, alpha, m_new [8], cz[4][8], zacc[2][8]
-  static constexpr int n_floats = 4 * 8 + 8 * 8 + 4 * 8 + 4 * 8 + 2 * 8;
+  // floats: red[4][8], redz[2][4][8], m_run, l_run, alpha, m_new [8], cz[4][8], zacc[2][8],
+  // cs[4][8]
+  static constexpr int n_floats = 4 * 8 + 8 * 8 + 4 * 8 + 4 * 8 + 2 * 8 + 4 * 8;
   static constexpr int cend_off = f_off + n_floats * 4;                        // [8] int64
-  static constexpr int bars_off = cend_off + 8 * 8;                            // 2 mbarriers, TMEM slot, flag
+  static constexpr int bars_off = cend_off + 8 * 8;                            // 2 mbarriers, TMEM slot, 2 flags
   static constexpr int raw_off = bars_off + 32;
   // staged words: K runs [128][rw] + 2, V runs [128][rw] + 2, key-group rows [3][2][65],
   // per-key value scale / zero [128][2][2]
@@ -217,10 +295,12 @@ __global__ void __launch_bounds__(attn::kThreadsA, 2) prefix_attention_sym(const
   float* m_new = alpha + NQ;
   float* cz = m_new + NQ;         // [4][NQ]: q . zero of the tile's key groups (block 3: 0)
   float* zacc = cz + 4 * NQ;      // [2][NQ]: running sum of p * value zero per channel group
+  float* cs = zacc + 2 * NQ;      // [4][NQ]: sum of q (.) scale (as rounded) of the tile's key groups
   int64_t* cend = reinterpret_cast<int64_t*>(sm + L::cend_off);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::bars_off);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 2);
   uint32_t* last_flag = tslot + 1;
+  uint32_t* fail_flag = tslot + 2;  // a softmax warp's wait for S ran out
   const int slot = a.slot_bits;
   const int rw = sym_run_words(slot);
   uint32_t* rawk = reinterpret_cast<uint32_t*>(sm + L::raw_off);  // [128][rw] + 2
@@ -243,7 +323,6 @@ __global__ void __launch_bounds__(attn::kThreadsA, 2) prefix_attention_sym(const
   constexpr uint32_t idesc_s = instr_desc(kBf16, kSymSCols) | (1u << 15);  // MN-major K tile
   constexpr uint32_t idesc_o = CODEC == 0 ? instr_desc(kBf16, kSymOCols) : (instr_desc(kBf16, kSymOCols) | (1u << 15));
   const int64_t C = static_cast<int64_t>(a.kv_heads) * kD;
-  const bool narrow = slot <= 4;
   const int64_t run = CODEC == 0 ? a.body : a.prefix;  // tokens per K (and KIVI V) dim run
   // value channel groups of this head (KIVI); KVQuant has one
   const int64_t cg_first = CODEC == 0 ? static_cast<int64_t>(h) * kD / a.group_size : 0;
@@ -254,9 +333,16 @@ __global__ void __launch_bounds__(attn::kThreadsA, 2) prefix_attention_sym(const
   const int u_lo = tid & 15, u_hi = tid >> 4;
   const uintptr_t s_lo[2] = {reinterpret_cast<uintptr_t>(a.stream[0]), reinterpret_cast<uintptr_t>(a.stream[1])};
   const uintptr_t s_hi[2] = {reinterpret_cast<uintptr_t>(a.stream_end[0]), reinterpret_cast<uintptr_t>(a.stream_end[1])};
-  const uint32_t rw_magic = (1u << 20) / static_cast<uint32_t>(rw) + 1u;  // e / rw == (e * rw_magic) >> 20, e < 4400
+  const float bias = sym_bias<kBf16>(slot);  // symbol tiles hold bias + s
+  const uint32_t mask4 = static_cast<uint32_t>(a.sym_mask & 0xF) * 0x01010101u;
+  // warps 4..7 stage: thread st = tid - 128 copies words e = st + 128 k of the [128][rw]
+  // staged runs, e = dim * rw + i advanced without division (128 = q128 * rw + r128)
+  constexpr int kStageThreads = kThreadsA / 2;
+  const int st = tid - kStageThreads;
+  const int q128 = kStageThreads / rw, r128 = kStageThreads % rw;
+  const int st_d0 = st >= 0 ? st / rw : 0, st_i0 = st >= 0 ? st % rw : 0;
 
-  // Stage the words tile kt decodes (all threads; one cp.async group). Per dim run, the
+  // Stage the words tile kt decodes (warps 4..7; one cp.async group per thread). Per dim run, the
   // 4 * slot + 1 words that hold the tile's 128 symbols (K; KIVI V) or the 512 * slot + 1
   // words of the head's 128 x 128 symbols (KVQuant V); the key groups' scale / zero rows
   // (KIVI); each body key's value scale / zero. Words outside a stream are skipped: their
@@ -265,32 +351,46 @@ __global__ void __launch_bounds__(attn::kThreadsA, 2) prefix_attention_sym(const
     const SymTile t = sym_tile<CODEC>(a, kt, kmax);
     if (!t.has_body) return;
     const int64_t koff = CODEC == 0 ? t.k0 - a.sink : t.k0;  // stream token of the tile's key 0
-    for (int e = tid; e < 128 * rw; e += kThreadsA) {
-      const int d = static_cast<int>((static_cast<uint32_t>(e) * rw_magic) >> 20);
-      const int i = e - d * rw;
-      const int64_t bit = static_cast<int64_t>(s_lo[0]) * 8 + ((static_cast<int64_t>(d) * a.kv_heads + h) * run + koff) * slot;
-      const uintptr_t wa = static_cast<uintptr_t>(bit >> 5) * 4 + 4u * static_cast<uint32_t>(i);
-      if (wa + 4 > s_lo[0] && wa < s_hi[0]) cp_async4(rawk + e, wa);
+    {  // K runs: dim d starts at bit s_lo * 8 + ((d * H + h) * run + koff) * slot
+      const int64_t step = static_cast<int64_t>(a.kv_heads) * run * slot;  // bits between dim runs
+      int64_t bit = static_cast<int64_t>(s_lo[0]) * 8 + (static_cast<int64_t>(st_d0 * a.kv_heads + h) * run + koff) * slot;
+      int i = st_i0;
+      for (int e = st; e < 128 * rw; e += kStageThreads) {
+        const uintptr_t wa = static_cast<uintptr_t>(bit >> 5) * 4 + 4u * static_cast<uint32_t>(i);
+        if (wa + 4 > s_lo[0] && wa < s_hi[0]) cp_async4(rawk + e, wa);
+        i += r128;
+        bit += q128 * step;
+        if (i >= rw) {
+          i -= rw;
+          bit += step;
+        }
+      }
     }
-    if (CODEC == 0) {
-      for (int e = tid; e < 128 * rw; e += kThreadsA) {
-        const int d = static_cast<int>((static_cast<uint32_t>(e) * rw_magic) >> 20);
-        const int i = e - d * rw;
-        const int64_t bit = static_cast<int64_t>(s_lo[1]) * 8 + ((static_cast<int64_t>(h) * kD + d) * a.body + koff) * slot;
+    if (CODEC == 0) {  // KIVI V runs: dim d starts at bit s_lo * 8 + ((h * 128 + d) * body + koff) * slot
+      const int64_t step = a.body * slot;
+      int64_t bit = static_cast<int64_t>(s_lo[1]) * 8 + ((static_cast<int64_t>(h) * kD + st_d0) * a.body + koff) * slot;
+      int i = st_i0;
+      for (int e = st; e < 128 * rw; e += kStageThreads) {
         const uintptr_t wa = static_cast<uintptr_t>(bit >> 5) * 4 + 4u * static_cast<uint32_t>(i);
         if (wa + 4 > s_lo[1] && wa < s_hi[1]) cp_async4(rawv + e, wa);
+        i += r128;
+        bit += q128 * step;
+        if (i >= rw) {
+          i -= rw;
+          bit += step;
+        }
       }
     } else {
       const int64_t bit = static_cast<int64_t>(s_lo[1]) * 8 + (static_cast<int64_t>(h) * a.prefix + t.k0) * kD * slot;
       const uintptr_t w0 = static_cast<uintptr_t>(bit >> 5) * 4;
       const int nw = 512 * slot + 1;
-      for (int e = tid; e < nw; e += kThreadsA) {
+      for (int e = st; e < nw; e += kStageThreads) {
         const uintptr_t wa = w0 + 4u * static_cast<uint32_t>(e);
         if (wa + 4 > s_lo[1] && wa < s_hi[1]) cp_async4(rawv + e, wa);
       }
     }
     if (CODEC == 0) {  // key group rows: [gi][scale, zero][65 words]
-      for (int e = tid; e < t.n_g * 2 * kMetaWords; e += kThreadsA) {
+      for (int e = st; e < t.n_g * 2 * kMetaWords; e += kStageThreads) {
         const int gi = e / (2 * kMetaWords), r = e - gi * 2 * kMetaWords;
         const int side = r >= kMetaWords ? 1 : 0, i = r - side * kMetaWords;
         const uintptr_t A = reinterpret_cast<uintptr_t>(side ? a.zero[0] : a.scale[0]) +
@@ -298,15 +398,17 @@ __global__ void __launch_bounds__(attn::kThreadsA, 2) prefix_attention_sym(const
         if (i < 64 + ((A & 3) ? 1 : 0)) cp_async4(kmw + e, (A & ~static_cast<uintptr_t>(3)) + 4u * i);
       }
     }
-    {  // value scale / zero of the body keys: key k0 + (tid & 127), side tid >> 7
-      const int tk = tid & 127, side = tid >> 7;
-      const int64_t key = t.k0 + tk;
+    {  // value scale / zero of the body keys: key k0 + st
+      const int64_t key = t.k0 + st;
       if (key >= t.b_lo && key < t.b_hi) {
         const int64_t idx = CODEC == 0 ? (key - a.sink) * vgroups + cg_first : key;
-        const uintptr_t A = reinterpret_cast<uintptr_t>(side ? a.zero[1] : a.scale[1]) + 2 * static_cast<uintptr_t>(idx);
-        const uintptr_t A4 = A & ~static_cast<uintptr_t>(3);
-        cp_async4(vmw + (tk * 2 + side) * 2, A4);
-        if ((A & 3) + 2 * (CODEC == 0 ? n_cg : 1) > 4) cp_async4(vmw + (tk * 2 + side) * 2 + 1, A4 + 4);
+#pragma unroll
+        for (int side = 0; side < 2; ++side) {
+          const uintptr_t A = reinterpret_cast<uintptr_t>(side ? a.zero[1] : a.scale[1]) + 2 * static_cast<uintptr_t>(idx);
+          const uintptr_t A4 = A & ~static_cast<uintptr_t>(3);
+          cp_async4(vmw + (st * 2 + side) * 2, A4);
+          if ((A & 3) + 2 * (CODEC == 0 ? n_cg : 1) > 4) cp_async4(vmw + (st * 2 + side) * 2 + 1, A4 + 4);
+        }
       }
     }
   };
@@ -315,14 +417,17 @@ __global__ void __launch_bounds__(attn::kThreadsA, 2) prefix_attention_sym(const
     mbar_init(&bars[0], 1);
     mbar_init(&bars[1], 1);
     fence_mbar_init();
+    *fail_flag = 0u;
   }
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(tslot)),
                  "r"(kSymTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n");
   }
-  if (t_begin < t_end) stage(t_begin);
-  cp_async_commit();
+  if (warp >= 4) {
+    if (t_begin < t_end) stage(t_begin);
+    cp_async_commit();
+  }
   // byte table, zeroed B blocks of the groups and channel groups, q rows (real block),
   // per-row causal ends, running sums
   lut[tid] = sym_lut_entry<QT>(static_cast<uint32_t>(tid), slot, static_cast<uint32_t>((1 << a.sym_len) - 1));
@@ -351,7 +456,7 @@ __global__ void __launch_bounds__(attn::kThreadsA, 2) prefix_attention_sym(const
     l_run[tid] = 0.f;
     cend[tid] = row < a.rows ? min(a.seq_len - 1, a.q_start + row / a.group) : -1;
   }
-  if (tid < 6 * NQ) cz[tid] = 0.f;  // cz and zacc
+  if (tid < 10 * NQ) cz[tid] = 0.f;  // cz, zacc, cs
   __syncthreads();
   // B operands of a key group: threads 0..127 write q (.) scale (one 8-dim chunk c of one
   // row n each), threads 128..255 sum q . zero over the row into cz
@@ -363,16 +468,21 @@ __global__ void __launch_bounds__(attn::kThreadsA, 2) prefix_attention_sym(const
     const uint4 qv = *reinterpret_cast<const uint4*>(bq_real + qb_c * kLBO + qb_n * 16);
     const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
     const uint32_t mw[4] = {mv.x, mv.y, mv.z, mv.w};
-    if (!zero_side) {
+    if (!zero_side) {  // q (.) scale, and its sum over the row (the bias of the symbols)
       uint32_t o[4];
+      float qs = 0.f;
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&mw[k]));
         const float q0 = bits_to_float(static_cast<uint16_t>(qw[k] & 0xFFFFu), kBf16);
         const float q1 = bits_to_float(static_cast<uint16_t>(qw[k] >> 16), kBf16);
         o[k] = pack2<QT>(q0 * f.x, q1 * f.y);
+        qs += bits_to_float(static_cast<uint16_t>(o[k] & 0xFFFFu), kBf16) + bits_to_float(static_cast<uint16_t>(o[k] >> 16), kBf16);
       }
       *reinterpret_cast<uint4*>(bq_sm + gi * kRowTile + qb_c * kLBO + qb_n * 16) = make_uint4(o[0], o[1], o[2], o[3]);
+#pragma unroll
+      for (int x = 1; x < 16; x <<= 1) qs += __shfl_xor_sync(0xffffffffu, qs, x);
+      if (qb_c == 0) cs[gi * NQ + qb_n] = qs;
     } else {
       float acc = 0.f;
 #pragma unroll
@@ -408,25 +518,33 @@ __global__ void __launch_bounds__(attn::kThreadsA, 2) prefix_attention_sym(const
     // K tile (MMA 1 of the previous tile has completed): body units from the staged runs
     // through the byte table, keys contiguous; other octets as 8 x 8 blocks transposed to
     // keys-contiguous
-    const int64_t kb_u = k0 + 8 * u_lo;  // the key octet of this thread's K and KIVI V units
-    const bool k_body = body_octet<CODEC>(a, kb_u, kmax);
-    if (k_body) {
-#pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        const int d = u_hi + 16 * r;
-        const uint32_t b0 = static_cast<uint32_t>(s_lo[0]) * 8u +
-                            (static_cast<uint32_t>(d * a.kv_heads + h) * static_cast<uint32_t>(run) + koff) *
-                                static_cast<uint32_t>(slot);
-        const Win w = staged_window(rawk + d * rw, (b0 & 31u) + 8u * static_cast<uint32_t>(u_lo * slot), narrow);
-        *reinterpret_cast<uint4*>(kt_sm + u_lo * kSBO + (d >> 3) * kLBO + (d & 7) * 16) = sym8(lut, w, slot);
-      }
+    // body octets of the tile (octet o = keys k0 + 8 o ..): [ob_lo, ob_hi)
+    const int ob_lo = static_cast<int>((t.b_lo - k0 + 7) >> 3);
+    const int ob_hi = t.has_body ? static_cast<int>((t.b_hi - k0) >> 3) : 0;
+    // this thread's body octets among octets 8 kh .. 8 kh + 7 of its dim dd
+    const int kh = tid >> 7, dd = tid & 127;
+    uint32_t octs = 0u;
+    {
+      const int lo = max(ob_lo - 8 * kh, 0), hi = min(ob_hi - 8 * kh, 8);
+      if (hi > lo) octs = ((0xFFu >> (8 - (hi - lo))) << lo) & 0xFFu;
+    }
+    if (octs) {
+      const uint32_t b0 = static_cast<uint32_t>(s_lo[0]) * 8u +
+                          (static_cast<uint32_t>(dd * a.kv_heads + h) * static_cast<uint32_t>(run) + koff) *
+                              static_cast<uint32_t>(slot);
+      const uint32_t pos0 = (b0 & 31u) + 64u * static_cast<uint32_t>(kh * slot);
+      const uint32_t* src = rawk + dd * rw + (pos0 >> 5);
+      uint8_t* dst = kt_sm + 8 * kh * kSBO + (dd >> 3) * kLBO + (dd & 7) * 16;
+      if (slot == 2) decode_half_run<2, kBf16>(src, pos0 & 31u, octs, dst, kSBO, lut, mask4);
+      else if (slot == 4) decode_half_run<4, kBf16>(src, pos0 & 31u, octs, dst, kSBO, lut, mask4);
+      else decode_half_run<8, kBf16>(src, pos0 & 31u, octs, dst, kSBO, lut, mask4);
     }
     {
       const int dq = u_lo, ko = u_hi;  // the 8 x 8 block (dims 8 dq.., keys 8 ko..) of this thread
       const int64_t kb = k0 + 8 * ko;
-      if (!body_octet<CODEC>(a, kb, kmax)) {
+      if (ko < ob_lo || ko >= ob_hi) {
         uint32_t m[8][4];
-        real_rows8<QT, CODEC>(a, 0, h, kb, dq, kmax, m);
+        real_rows8<QT, CODEC>(a, 0, h, kb, dq, kmax, bias, m);
         transpose8x8_u16(m);  // rows per dim
 #pragma unroll
         for (int i = 0; i < 8; ++i)
@@ -443,35 +561,6 @@ __global__ void __launch_bounds__(attn::kThreadsA, 2) prefix_attention_sym(const
                                              __funnelshift_r(w[2], w[3], 16), __funnelshift_r(w[3], w[4], 16))
                                 : make_uint4(w[0], w[1], w[2], w[3]);
           build_qb(gi, mv);
-        }
-      }
-    }
-    // V windows from the staged runs, before waiting for MMA 2 of the previous tile
-    Win w[8];
-    uint32_t v_take = 0u;
-#pragma unroll
-    for (int r = 0; r < 8; ++r) w[r].lo = w[r].hi = 0u;
-    if (CODEC == 0) {
-      if (k_body) {
-        v_take = 0xFFu;
-#pragma unroll
-        for (int r = 0; r < 8; ++r) {
-          const int d = u_hi + 16 * r;
-          const uint32_t b0 = static_cast<uint32_t>(s_lo[1]) * 8u +
-                              (static_cast<uint32_t>(h * kD + d) * static_cast<uint32_t>(a.body) + koff) *
-                                  static_cast<uint32_t>(slot);
-          w[r] = staged_window(rawv + d * rw, (b0 & 31u) + 8u * static_cast<uint32_t>(u_lo * slot), narrow);
-        }
-      }
-    } else {
-      const uint32_t b0 = static_cast<uint32_t>(s_lo[1]) * 8u +
-                          static_cast<uint32_t>((static_cast<int64_t>(h) * a.prefix + k0) * kD) * static_cast<uint32_t>(slot);
-#pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        const int tl = u_hi + 16 * r;
-        if (body_octet<CODEC>(a, k0 + (tl & ~7), kmax)) {
-          v_take |= 1u << r;
-          w[r] = staged_window(rawv, (b0 & 31u) + static_cast<uint32_t>((tl * kD + 8 * u_lo) * slot), narrow);
         }
       }
     }
@@ -505,25 +594,33 @@ __global__ void __launch_bounds__(attn::kThreadsA, 2) prefix_attention_sym(const
         break;
       }
     }
-    // V^T tile: KIVI K-major (rows per dim, keys contiguous), KVQuant MN-major (dims
-    // contiguous per key)
-#pragma unroll
-    for (int r = 0; r < 8; ++r) {
-      if (!((v_take >> r) & 1u)) continue;
-      if (CODEC == 0) {
-        const int d = u_hi + 16 * r;
-        *reinterpret_cast<uint4*>(vt_sm + (d >> 3) * kSBO + u_lo * kLBO + (d & 7) * 16) = sym8(lut, w[r], slot);
-      } else {
-        const int tl = u_hi + 16 * r;
-        *reinterpret_cast<uint4*>(vt_sm + u_lo * kSBO + (tl >> 3) * kLBO + (tl & 7) * 16) = sym8(lut, w[r], slot);
+    // V^T tile from the staged words: KIVI K-major (one dim run per thread, keys
+    // contiguous), KVQuant MN-major (dim octet u_lo of keys u_hi + 16 r)
+    if (CODEC == 0) {
+      if (octs) {
+        const uint32_t b0 = static_cast<uint32_t>(s_lo[1]) * 8u +
+                            (static_cast<uint32_t>(h * kD + dd) * static_cast<uint32_t>(a.body) + koff) *
+                                static_cast<uint32_t>(slot);
+        const uint32_t pos0 = (b0 & 31u) + 64u * static_cast<uint32_t>(kh * slot);
+        const uint32_t* src = rawv + dd * rw + (pos0 >> 5);
+        uint8_t* dst = vt_sm + (dd >> 3) * kSBO + 8 * kh * kLBO + (dd & 7) * 16;
+        if (slot == 2) decode_half_run<2, kBf16>(src, pos0 & 31u, octs, dst, kLBO, lut, mask4);
+        else if (slot == 4) decode_half_run<4, kBf16>(src, pos0 & 31u, octs, dst, kLBO, lut, mask4);
+        else decode_half_run<8, kBf16>(src, pos0 & 31u, octs, dst, kLBO, lut, mask4);
       }
+    } else if (ob_hi > ob_lo) {
+      const uint32_t b0 = static_cast<uint32_t>(s_lo[1]) * 8u +
+                          static_cast<uint32_t>((static_cast<int64_t>(h) * a.prefix + k0) * kD) * static_cast<uint32_t>(slot);
+      if (slot == 2) decode_kvq_v<2, kBf16>(rawv, b0 & 31u, u_lo, u_hi, ob_lo, ob_hi, vt_sm, lut, mask4);
+      else if (slot == 4) decode_kvq_v<4, kBf16>(rawv, b0 & 31u, u_lo, u_hi, ob_lo, ob_hi, vt_sm, lut, mask4);
+      else decode_kvq_v<8, kBf16>(rawv, b0 & 31u, u_lo, u_hi, ob_lo, ob_hi, vt_sm, lut, mask4);
     }
     {
       const int dq = u_lo, ko = u_hi;
       const int64_t kb = k0 + 8 * ko;
-      if (!body_octet<CODEC>(a, kb, kmax)) {
+      if (ko < ob_lo || ko >= ob_hi) {
         uint32_t m[8][4];
-        real_rows8<QT, CODEC>(a, 1, h, kb, dq, kmax, m);  // rows per key
+        real_rows8<QT, CODEC>(a, 1, h, kb, dq, kmax, bias, m);  // rows per key
         if (CODEC == 0) transpose8x8_u16(m);              // K-major V^T: rows per dim
 #pragma unroll
         for (int i = 0; i < 8; ++i)
@@ -541,19 +638,19 @@ __global__ void __launch_bounds__(attn::kThreadsA, 2) prefix_attention_sym(const
                 s > 0 ? 1u : 0u);
       mma_commit(&bars[0]);
     }
-    if (kt + 1 < t_end) stage(kt + 1);
-    cp_async_commit();
-    {
-      const bool ok = mbar_wait_bounded(&bars[0], ph1);
-      ph1 ^= 1u;
-      if (__syncthreads_or(!ok)) {
-        failed = true;
-        break;
-      }
+    // warps 4..7 stage tile kt + 1 while warps 0..3 wait for S and run the softmax
+    bool s_ok = true;
+    if (warp >= 4) {
+      if (kt + 1 < t_end) stage(kt + 1);
+      cp_async_commit();
+    } else {
+      s_ok = !named_sync_or_softmax(!mbar_wait_bounded(&bars[0], ph1));
+      if (!s_ok && tid == 0) *fail_flag = 1u;
+      tc_fence_after();
     }
-    tc_fence_after();
+    ph1 ^= 1u;
 
-    if (warp < 4) {
+    if (warp < 4 && s_ok) {
       // S^T row of this key from its block (the same columns of every block are loaded by
       // the whole warp, then each lane keeps its own), plus q . zero of its key group
       float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
@@ -573,7 +670,7 @@ __global__ void __launch_bounds__(attn::kThreadsA, 2) prefix_attention_sym(const
       }
       if (blk < kSymReal)
 #pragma unroll
-        for (int n = 0; n < 8; ++n) s[n] += cz[blk * NQ + n];
+        for (int n = 0; n < 8; ++n) s[n] += cz[blk * NQ + n] - bias * cs[blk * NQ + n];
       float x[8];
 #pragma unroll
       for (int n = 0; n < 8; ++n) x[n] = key <= cend[n] ? s[n] * a.scale_log2 : -INFINITY;
@@ -591,16 +688,24 @@ __global__ void __launch_bounds__(attn::kThreadsA, 2) prefix_attention_sym(const
         m_new[tid] = mn;
       }
       named_sync_softmax();
+      // P (.) vscale_c into the B operand; per row, sum p * vzero minus bias times the
+      // rounded P (.) vscale of the body keys (their V values carry the bias)
+      const float kbias = blk == kSymReal ? 0.f : bias;
       float p[8], z0[8], z1[8];
 #pragma unroll
       for (int n = 0; n < 8; ++n) {
         p[n] = x[n] == -INFINITY ? 0.f : exp2f(x[n] - m_new[n]);
-        z0[n] = p[n] * vze[0];
-        z1[n] = p[n] * vze[1];
+        float pr[kSymMaxC] = {0.f, 0.f};
 #pragma unroll
-        for (int c = 0; c < kSymMaxC; ++c)
-          if (c < n_cg)
-            *reinterpret_cast<uint16_t*>(ps_sm + c * kRowTile + tile_off(n, tid)) = from_float<QT>(p[n] * vsc[c]);
+        for (int c = 0; c < kSymMaxC; ++c) {
+          if (c < n_cg) {
+            const uint16_t u = from_float<QT>(p[n] * vsc[c]);
+            *reinterpret_cast<uint16_t*>(ps_sm + c * kRowTile + tile_off(n, tid)) = u;
+            pr[c] = bits_to_float(u, kBf16);
+          }
+        }
+        z0[n] = __fmaf_rn(p[n], vze[0], -kbias * pr[0]);
+        z1[n] = __fmaf_rn(p[n], vze[1], -kbias * pr[1]);
       }
       {
         const float r = warp_reduce8<false>(p, lane);
@@ -623,6 +728,10 @@ __global__ void __launch_bounds__(attn::kThreadsA, 2) prefix_attention_sym(const
       }
     }
     const bool rescale = __syncthreads_or(tid < NQ && alpha[tid] != 1.f) && j > 0;
+    if (*fail_flag) {
+      failed = true;
+      break;
+    }
     if (warp >= 4 && rescale) {
       for (int c = 0; c < n_cg; ++c) {
         float o[8];
