@@ -81,6 +81,9 @@ LARGE = [
                    query_heads=32, query_start=33023, seq_len=33024),
     attention_case("kvquant_b4_8k_q16_bf16", 502, codec=1, bits=4, prefix=8192, kv_heads=8, query_heads=32,
                    query_tokens=16, query_start=8300, query_bf16=True),
+    # the bench's ATTN layer shape on the symbol-operand kernel (group 64, staged stream words)
+    attention_case("kivi_b2_g64_32k_decode", 503, codec=0, bits=2, prefix=32768, sink=128, group_size=64, kv_heads=8,
+                   query_heads=32, query_start=33023, seq_len=33024, query_bf16=True),
 ]
 
 
