@@ -292,6 +292,8 @@ int32_t origami_kivi_dequantize_to_kv_cache(
   if ((rc = check_blocks(cache, d_block_ids, num_block_ids, tokens))) return rc;
   if (channels > 0x7FFFFFFF || cache->head_dim > 0x7FFFFFFF)
     return fail(ORIGAMI_ERR_UNSUPPORTED, "heads * head_dim must be below 2^31");
+  if (tokens > 0x7FFFFFFF || cache->block_size > 0x7FFFFFFF)
+    return fail(ORIGAMI_ERR_UNSUPPORTED, "tokens and block_size must be below 2^31");
 
   origami::KiviArgs a{};
   a.stream[0] = d_bytestream + key_offset;

@@ -423,7 +423,7 @@ __global__ void __launch_bounds__(kThreads) kivi_to_cache(const __grid_constant_
       const int64_t t = t0 + r;
       int64_t off = -1;
       if (t < a.tokens) {
-        const int64_t bi = t / a.block_size;
+        const int64_t bi = static_cast<uint32_t>(t) / static_cast<uint32_t>(a.block_size);  // both below 2^31
         const int64_t blk = a.ids[bi];
         if (blk < 0 || blk >= a.num_blocks) {
           if (a.err) atomicAdd(a.err, 1u);
@@ -440,10 +440,13 @@ __global__ void __launch_bounds__(kThreads) kivi_to_cache(const __grid_constant_
       const uint8_t* s = a.stream[kv];
       const uintptr_t end = reinterpret_cast<uintptr_t>(s) + static_cast<uintptr_t>(a.stream_bytes[kv]);
       const int words = ((nbody * bits + 7) >> 3) / 4 + 2;
+      // word i = d * words + w of the staged runs, walked without division: consecutive
+      // dims' runs are dstep bits apart (key runs: H * body symbols; value runs: body)
+      const int64_t dstep = static_cast<int64_t>(kv ? 1 : a.H) * a.body_tokens * bits;
+      const int qd = kThreads / words, rw = kThreads % words;
+      int d = tid / words, w = tid - (tid / words) * words;
+      int64_t bitpos = kivi_index(a, kv, h, d, tb0 - a.sink_tokens) * bits;
       for (int i = tid; i < D * words; i += kThreads) {
-        const int d = i / words;
-        const int w = i - d * words;
-        const int64_t bitpos = kivi_index(a, kv, h, d, tb0 - a.sink_tokens) * bits;
         const uintptr_t first = reinterpret_cast<uintptr_t>(s) + static_cast<uintptr_t>(bitpos >> 3);
         const uintptr_t wa = (first & ~static_cast<uintptr_t>(3)) + 4u * static_cast<uintptr_t>(w);
         uint32_t v = 0;
@@ -453,6 +456,14 @@ __global__ void __launch_bounds__(kThreads) kivi_to_cache(const __grid_constant_
         }
         reinterpret_cast<uint32_t*>(runs + d * G::rs)[w] = v;
         if (w == 0) bit0[d] = static_cast<int32_t>((first & 3u) * 8u + static_cast<uintptr_t>(bitpos & 7));
+        w += rw;
+        d += qd;
+        bitpos += qd * dstep;
+        if (w >= words) {
+          w -= words;
+          d += 1;
+          bitpos += dstep;
+        }
       }
     }
     // UNI: this tile's scale / zero, coalesced into shared memory when they fit in
