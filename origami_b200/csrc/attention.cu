@@ -125,15 +125,24 @@ int32_t workspace_plan(int64_t query_tokens, int64_t query_heads, int64_t kv_hea
   return ORIGAMI_OK;
 }
 
-template <typename QT, int CODEC>
-int32_t launch_sym(const origami::AttnArgs& a, int64_t ctas, cudaStream_t st) {
-  const void* fn = reinterpret_cast<const void*>(&origami::prefix_attention_sym<QT, CODEC>);
-  const int smem = origami::AttnSymSmem::bytes(a.slot_bits);
+template <typename QT, int CODEC, int SLOT>
+int32_t launch_sym_slot(const origami::AttnArgs& a, int64_t ctas, cudaStream_t st) {
+  const void* fn = reinterpret_cast<const void*>(&origami::prefix_attention_sym<QT, CODEC, SLOT>);
+  constexpr int smem = origami::AttnSymSmem::bytes(SLOT);
   int resident = 0;
   int32_t rc = persistent_slots(fn, smem, resident);  // raises the kernel's shared-memory limit
   if (rc) return rc;
-  origami::prefix_attention_sym<QT, CODEC><<<static_cast<unsigned>(ctas), origami::attn::kThreadsA, smem, st>>>(a);
+  origami::prefix_attention_sym<QT, CODEC, SLOT><<<static_cast<unsigned>(ctas), origami::attn::kThreadsA, smem, st>>>(a);
   return after_launch("prefix_attention_sym launch");
+}
+
+template <typename QT, int CODEC>
+int32_t launch_sym(const origami::AttnArgs& a, int64_t ctas, cudaStream_t st) {
+  switch (a.slot_bits) {
+    case 2: return launch_sym_slot<QT, CODEC, 2>(a, ctas, st);
+    case 4: return launch_sym_slot<QT, CODEC, 4>(a, ctas, st);
+    default: return launch_sym_slot<QT, CODEC, 8>(a, ctas, st);
+  }
 }
 
 int64_t packed_symbol_bytes(int64_t bits, int64_t symbols) {

@@ -274,8 +274,8 @@ static_assert(AttnSymSmem::raw_off % 16 == 0, "staged words 16-byte aligned");
 static_assert(AttnSymSmem::bytes(4) + 1024 <= 233472 / 2, "two CTAs per SM up to 4-bit slots");
 
 // grid = kv_heads * row_blocks * splits CTAs of 256 threads, 8 query rows per CTA; dynamic
-// shared memory AttnSymSmem::bytes(slot_bits).
-template <typename QT, int CODEC>
+// shared memory AttnSymSmem::bytes(SLOT). SLOT = a.slot_bits (2, 4 or 8).
+template <typename QT, int CODEC, int SLOT>
 __global__ void __launch_bounds__(attn::kThreadsA, 2) prefix_attention_sym(const __grid_constant__ AttnArgs a) {
   using namespace attn;
   using L = AttnSymSmem;
@@ -301,8 +301,8 @@ __global__ void __launch_bounds__(attn::kThreadsA, 2) prefix_attention_sym(const
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 2);
   uint32_t* last_flag = tslot + 1;
   uint32_t* fail_flag = tslot + 2;  // a softmax warp's wait for S ran out
-  const int slot = a.slot_bits;
-  const int rw = sym_run_words(slot);
+  constexpr int slot = SLOT;
+  constexpr int rw = sym_run_words(SLOT);
   uint32_t* rawk = reinterpret_cast<uint32_t*>(sm + L::raw_off);  // [128][rw] + 2
   uint32_t* rawv = rawk + 128 * rw + 2;                           // [128][rw] + 2 (KVQuant: one run)
   uint32_t* kmw = rawv + 128 * rw + 2;                            // [3][2][65]
@@ -331,15 +331,16 @@ __global__ void __launch_bounds__(attn::kThreadsA, 2) prefix_attention_sym(const
   // this thread's fill units: K and KIVI V: key octet tid & 15 of dims (tid >> 4) + 16 r;
   // KVQuant V: dim octet tid & 15 of keys (tid >> 4) + 16 r
   const int u_lo = tid & 15, u_hi = tid >> 4;
-  const uintptr_t s_lo[2] = {reinterpret_cast<uintptr_t>(a.stream[0]), reinterpret_cast<uintptr_t>(a.stream[1])};
-  const uintptr_t s_hi[2] = {reinterpret_cast<uintptr_t>(a.stream_end[0]), reinterpret_cast<uintptr_t>(a.stream_end[1])};
-  const float bias = sym_bias<kBf16>(slot);  // symbol tiles hold bias + s
+  // stream bounds are read from the parameters where used (no registers held across the loop)
+#define SYM_S_LO(k) reinterpret_cast<uintptr_t>(a.stream[k])
+#define SYM_S_HI(k) reinterpret_cast<uintptr_t>(a.stream_end[k])
+  constexpr float bias = sym_bias<kBf16>(SLOT);  // symbol tiles hold bias + s
   const uint32_t mask4 = static_cast<uint32_t>(a.sym_mask & 0xF) * 0x01010101u;
   // warps 4..7 stage: thread st = tid - 128 copies words e = st + 128 k of the [128][rw]
   // staged runs, e = dim * rw + i advanced without division (128 = q128 * rw + r128)
   constexpr int kStageThreads = kThreadsA / 2;
   const int st = tid - kStageThreads;
-  const int q128 = kStageThreads / rw, r128 = kStageThreads % rw;
+  constexpr int q128 = kStageThreads / rw, r128 = kStageThreads % rw;
   const int st_d0 = st >= 0 ? st / rw : 0, st_i0 = st >= 0 ? st % rw : 0;
 
   // Stage the words tile kt decodes (warps 4..7; one cp.async group per thread). Per dim run, the
@@ -353,11 +354,12 @@ __global__ void __launch_bounds__(attn::kThreadsA, 2) prefix_attention_sym(const
     const int64_t koff = CODEC == 0 ? t.k0 - a.sink : t.k0;  // stream token of the tile's key 0
     {  // K runs: dim d starts at bit s_lo * 8 + ((d * H + h) * run + koff) * slot
       const int64_t step = static_cast<int64_t>(a.kv_heads) * run * slot;  // bits between dim runs
-      int64_t bit = static_cast<int64_t>(s_lo[0]) * 8 + (static_cast<int64_t>(st_d0 * a.kv_heads + h) * run + koff) * slot;
+      int64_t bit = static_cast<int64_t>(SYM_S_LO(0)) * 8 + (static_cast<int64_t>(st_d0 * a.kv_heads + h) * run + koff) * slot;
       int i = st_i0;
+#pragma unroll 1
       for (int e = st; e < 128 * rw; e += kStageThreads) {
         const uintptr_t wa = static_cast<uintptr_t>(bit >> 5) * 4 + 4u * static_cast<uint32_t>(i);
-        if (wa + 4 > s_lo[0] && wa < s_hi[0]) cp_async4(rawk + e, wa);
+        if (wa + 4 > SYM_S_LO(0) && wa < SYM_S_HI(0)) cp_async4(rawk + e, wa);
         i += r128;
         bit += q128 * step;
         if (i >= rw) {
@@ -368,11 +370,12 @@ __global__ void __launch_bounds__(attn::kThreadsA, 2) prefix_attention_sym(const
     }
     if (CODEC == 0) {  // KIVI V runs: dim d starts at bit s_lo * 8 + ((h * 128 + d) * body + koff) * slot
       const int64_t step = a.body * slot;
-      int64_t bit = static_cast<int64_t>(s_lo[1]) * 8 + ((static_cast<int64_t>(h) * kD + st_d0) * a.body + koff) * slot;
+      int64_t bit = static_cast<int64_t>(SYM_S_LO(1)) * 8 + ((static_cast<int64_t>(h) * kD + st_d0) * a.body + koff) * slot;
       int i = st_i0;
+#pragma unroll 1
       for (int e = st; e < 128 * rw; e += kStageThreads) {
         const uintptr_t wa = static_cast<uintptr_t>(bit >> 5) * 4 + 4u * static_cast<uint32_t>(i);
-        if (wa + 4 > s_lo[1] && wa < s_hi[1]) cp_async4(rawv + e, wa);
+        if (wa + 4 > SYM_S_LO(1) && wa < SYM_S_HI(1)) cp_async4(rawv + e, wa);
         i += r128;
         bit += q128 * step;
         if (i >= rw) {
@@ -381,15 +384,17 @@ __global__ void __launch_bounds__(attn::kThreadsA, 2) prefix_attention_sym(const
         }
       }
     } else {
-      const int64_t bit = static_cast<int64_t>(s_lo[1]) * 8 + (static_cast<int64_t>(h) * a.prefix + t.k0) * kD * slot;
+      const int64_t bit = static_cast<int64_t>(SYM_S_LO(1)) * 8 + (static_cast<int64_t>(h) * a.prefix + t.k0) * kD * slot;
       const uintptr_t w0 = static_cast<uintptr_t>(bit >> 5) * 4;
       const int nw = 512 * slot + 1;
+#pragma unroll 1
       for (int e = st; e < nw; e += kStageThreads) {
         const uintptr_t wa = w0 + 4u * static_cast<uint32_t>(e);
-        if (wa + 4 > s_lo[1] && wa < s_hi[1]) cp_async4(rawv + e, wa);
+        if (wa + 4 > SYM_S_LO(1) && wa < SYM_S_HI(1)) cp_async4(rawv + e, wa);
       }
     }
     if (CODEC == 0) {  // key group rows: [gi][scale, zero][65 words]
+#pragma unroll 1
       for (int e = st; e < t.n_g * 2 * kMetaWords; e += kStageThreads) {
         const int gi = e / (2 * kMetaWords), r = e - gi * 2 * kMetaWords;
         const int side = r >= kMetaWords ? 1 : 0, i = r - side * kMetaWords;
@@ -430,7 +435,8 @@ __global__ void __launch_bounds__(attn::kThreadsA, 2) prefix_attention_sym(const
   }
   // byte table, zeroed B blocks of the groups and channel groups, q rows (real block),
   // per-row causal ends, running sums
-  lut[tid] = sym_lut_entry<QT>(static_cast<uint32_t>(tid), slot, static_cast<uint32_t>((1 << a.sym_len) - 1));
+  if constexpr (kBf16 && SLOT == 8)  // the byte table serves bf16 8-bit symbols only
+    lut[tid] = sym_lut_entry<QT>(static_cast<uint32_t>(tid), slot, static_cast<uint32_t>((1 << a.sym_len) - 1));
   for (int e = tid; e < (kSymMaxG * kRowTile) / 16; e += kThreadsA)
     reinterpret_cast<uint4*>(bq_sm)[e] = make_uint4(0u, 0u, 0u, 0u);
   for (int e = tid; e < (kSymMaxC * kRowTile) / 16; e += kThreadsA)
@@ -529,15 +535,13 @@ __global__ void __launch_bounds__(attn::kThreadsA, 2) prefix_attention_sym(const
       if (hi > lo) octs = ((0xFFu >> (8 - (hi - lo))) << lo) & 0xFFu;
     }
     if (octs) {
-      const uint32_t b0 = static_cast<uint32_t>(s_lo[0]) * 8u +
+      const uint32_t b0 = static_cast<uint32_t>(SYM_S_LO(0)) * 8u +
                           (static_cast<uint32_t>(dd * a.kv_heads + h) * static_cast<uint32_t>(run) + koff) *
                               static_cast<uint32_t>(slot);
       const uint32_t pos0 = (b0 & 31u) + 64u * static_cast<uint32_t>(kh * slot);
       const uint32_t* src = rawk + dd * rw + (pos0 >> 5);
       uint8_t* dst = kt_sm + 8 * kh * kSBO + (dd >> 3) * kLBO + (dd & 7) * 16;
-      if (slot == 2) decode_half_run<2, kBf16>(src, pos0 & 31u, octs, dst, kSBO, lut, mask4);
-      else if (slot == 4) decode_half_run<4, kBf16>(src, pos0 & 31u, octs, dst, kSBO, lut, mask4);
-      else decode_half_run<8, kBf16>(src, pos0 & 31u, octs, dst, kSBO, lut, mask4);
+      decode_half_run<SLOT, kBf16>(src, pos0 & 31u, octs, dst, kSBO, lut, mask4);
     }
     {
       const int dq = u_lo, ko = u_hi;  // the 8 x 8 block (dims 8 dq.., keys 8 ko..) of this thread
@@ -598,22 +602,18 @@ __global__ void __launch_bounds__(attn::kThreadsA, 2) prefix_attention_sym(const
     // contiguous), KVQuant MN-major (dim octet u_lo of keys u_hi + 16 r)
     if (CODEC == 0) {
       if (octs) {
-        const uint32_t b0 = static_cast<uint32_t>(s_lo[1]) * 8u +
+        const uint32_t b0 = static_cast<uint32_t>(SYM_S_LO(1)) * 8u +
                             (static_cast<uint32_t>(h * kD + dd) * static_cast<uint32_t>(a.body) + koff) *
                                 static_cast<uint32_t>(slot);
         const uint32_t pos0 = (b0 & 31u) + 64u * static_cast<uint32_t>(kh * slot);
         const uint32_t* src = rawv + dd * rw + (pos0 >> 5);
         uint8_t* dst = vt_sm + (dd >> 3) * kSBO + 8 * kh * kLBO + (dd & 7) * 16;
-        if (slot == 2) decode_half_run<2, kBf16>(src, pos0 & 31u, octs, dst, kLBO, lut, mask4);
-        else if (slot == 4) decode_half_run<4, kBf16>(src, pos0 & 31u, octs, dst, kLBO, lut, mask4);
-        else decode_half_run<8, kBf16>(src, pos0 & 31u, octs, dst, kLBO, lut, mask4);
+        decode_half_run<SLOT, kBf16>(src, pos0 & 31u, octs, dst, kLBO, lut, mask4);
       }
     } else if (ob_hi > ob_lo) {
-      const uint32_t b0 = static_cast<uint32_t>(s_lo[1]) * 8u +
+      const uint32_t b0 = static_cast<uint32_t>(SYM_S_LO(1)) * 8u +
                           static_cast<uint32_t>((static_cast<int64_t>(h) * a.prefix + k0) * kD) * static_cast<uint32_t>(slot);
-      if (slot == 2) decode_kvq_v<2, kBf16>(rawv, b0 & 31u, u_lo, u_hi, ob_lo, ob_hi, vt_sm, lut, mask4);
-      else if (slot == 4) decode_kvq_v<4, kBf16>(rawv, b0 & 31u, u_lo, u_hi, ob_lo, ob_hi, vt_sm, lut, mask4);
-      else decode_kvq_v<8, kBf16>(rawv, b0 & 31u, u_lo, u_hi, ob_lo, ob_hi, vt_sm, lut, mask4);
+      decode_kvq_v<SLOT, kBf16>(rawv, b0 & 31u, u_lo, u_hi, ob_lo, ob_hi, vt_sm, lut, mask4);
     }
     {
       const int dq = u_lo, ko = u_hi;
@@ -822,6 +822,8 @@ __global__ void __launch_bounds__(attn::kThreadsA, 2) prefix_attention_sym(const
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(kSymTmemCols));
   }
+#undef SYM_S_LO
+#undef SYM_S_HI
 }
 
 }  // namespace origami
