@@ -159,6 +159,20 @@ __device__ __forceinline__ uint4 lookup8_shfl(uint32_t lut, uint64_t field, int 
   return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
+// One (kv, token) row of BITS-bit symbols (BITS <= 5) by shuffle lookups: lane l's vectors
+// v = l, l + 32, ... of eight symbols each, one 16-byte store per vector. The constant
+// width turns every field shift and mask into an immediate.
+template <int BITS, typename OUT>
+__device__ __forceinline__ void cg_row_shfl(const uint8_t* s, int64_t nb, int64_t k0, int nvec, uint32_t lut, OUT* dst,
+                                            int lane) {
+  for (int v0 = 0; v0 < nvec; v0 += 32) {
+    const int v = v0 + lane;
+    const uint64_t field = v < nvec ? symbols8_raw(s, nb, k0 + v, BITS) : 0;
+    const uint4 out = lookup8_shfl(lut, field, BITS);
+    if (v < nvec) st_global_cs16(dst + 8 * v, out);
+  }
+}
+
 // A warp per (kv, token) row; VEC: eight symbols -> one 16-byte store per lane step.
 // Symbols of up to 5 bits (every CacheGen bins setting of the reference,
 // cachegen_adapter.py:49-57) are dequantized by shuffle: each lane computes the finished
@@ -190,11 +204,13 @@ __global__ void __launch_bounds__(kThreads) cachegen_to_cache(const __grid_const
     if constexpr (VEC) {
       if (bits <= 5) {
         const uint32_t lut = out_bits<OUT>(table[kv][lane] * m);
-        for (int v0 = 0; v0 < a.nvec; v0 += 32) {
-          const int v = v0 + lane;
-          const uint64_t field = v < a.nvec ? symbols8_raw(s, nb, t * a.nvec + v, bits) : 0;
-          const uint4 out = lookup8_shfl(lut, field, bits);
-          if (v < a.nvec) st_global_cs16(dst + 8 * v, out);
+        const int64_t k0 = t * a.nvec;
+        switch (bits) {  // warp-uniform
+          case 5: cg_row_shfl<5, OUT>(s, nb, k0, a.nvec, lut, dst, lane); break;
+          case 4: cg_row_shfl<4, OUT>(s, nb, k0, a.nvec, lut, dst, lane); break;
+          case 3: cg_row_shfl<3, OUT>(s, nb, k0, a.nvec, lut, dst, lane); break;
+          case 2: cg_row_shfl<2, OUT>(s, nb, k0, a.nvec, lut, dst, lane); break;
+          default: cg_row_shfl<1, OUT>(s, nb, k0, a.nvec, lut, dst, lane); break;
         }
       } else {
         for (int v = lane; v < a.nvec; v += 32)
