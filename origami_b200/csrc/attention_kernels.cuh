@@ -611,66 +611,84 @@ __device__ __forceinline__ void named_sync_softmax() { asm volatile("bar.sync 1,
 
 }  // namespace attn
 
-// Merge of the splits of one row block by the CTA that finished last. One warp per row
-// turns the splits' (max, sum) into weights exp2(max_s - max) / sum in `stage` (splits * NQ
-// floats of free shared memory); then each thread accumulates NQ / 8 float4 of O over the
-// splits, 8 float4 loads in flight.
+// Merge of the splits of one row block by the CTA that finished last. The first round of
+// partial-O loads goes out before the weights: one warp per row turns the splits' (max,
+// sum) into weights exp2(max_s - max) / sum in `stage` (splits * NQ floats of free shared
+// memory); each thread then accumulates NQ / 8 float4 of O over the splits, 16 float4
+// loads in flight.
 template <typename QT, int NQ>
 __device__ __forceinline__ void split_merge(const AttnArgs& a, int h, int rb, int row0, float* stage) {
   using namespace attn;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   __threadfence();
   const int64_t blk0 = (static_cast<int64_t>(h) * a.row_blocks + rb) * a.splits;
+  constexpr int kPer = NQ * kD / 4 / kThreadsA;  // float4 of O per thread
+  constexpr int kU = kPer >= 16 ? 1 : 16 / kPer;  // splits per round
+  constexpr int kSplit4 = NQ * kD / 4;            // float4 per split
+  const float4* o = reinterpret_cast<const float4*>(a.ws_o + blk0 * NQ * kD);
+  float4 v[kPer][kU];
+#pragma unroll
+  for (int k = 0; k < kPer; ++k)
+#pragma unroll
+    for (int u = 0; u < kU; ++u)
+      v[k][u] = u < a.splits ? __ldcg(o + static_cast<int64_t>(u) * kSplit4 + tid + k * kThreadsA)
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
   float* w_sm = stage;  // [splits][NQ]
   for (int n = warp; n < NQ; n += kThreadsA / 32) {
+    // (max, sum) of splits lane + 32 i, loaded once (splits <= 4096 / NQ <= 512)
+    constexpr int kMl = (4096 / NQ + 31) / 32;
+    float2 ml[kMl];
     float mx = -INFINITY;
-    for (int s2 = lane; s2 < a.splits; s2 += 32) mx = fmaxf(mx, __ldcg(a.ws_ml + ((blk0 + s2) * NQ + n) * 2));
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    float sum = 0.f;
-    for (int s2 = lane; s2 < a.splits; s2 += 32) {
-      const float ms = __ldcg(a.ws_ml + ((blk0 + s2) * NQ + n) * 2);
-      const float w = ms == -INFINITY ? 0.f : exp2f(ms - mx);
-      sum += w * __ldcg(a.ws_ml + ((blk0 + s2) * NQ + n) * 2 + 1);
-      w_sm[s2 * NQ + n] = w;
+    for (int i = 0; i < kMl; ++i) {
+      const int s2 = lane + 32 * i;
+      ml[i] = s2 < a.splits ? __ldcg(reinterpret_cast<const float2*>(a.ws_ml) + (blk0 + s2) * NQ + n)
+                            : make_float2(-INFINITY, 0.f);
+      mx = fmaxf(mx, ml[i].x);
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    for (int x = 16; x > 0; x >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, x));
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < kMl; ++i) {
+      const int s2 = lane + 32 * i;
+      if (s2 < a.splits) {
+        const float w = ml[i].x == -INFINITY ? 0.f : exp2f(ml[i].x - mx);
+        sum += w * ml[i].y;
+        w_sm[s2 * NQ + n] = w;
+      }
+    }
+#pragma unroll
+    for (int x = 16; x > 0; x >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, x);
     const float inv = 1.f / sum;
     __syncwarp();
     for (int s2 = lane; s2 < a.splits; s2 += 32) w_sm[s2 * NQ + n] *= inv;
   }
   __syncthreads();
-  constexpr int kPer = NQ * kD / 4 / kThreadsA;  // float4 of O per thread
-  constexpr int kU = kPer >= 8 ? 1 : 8 / kPer;   // splits per round
+  auto fma4 = [](float4& c, const float4& x, float w) {
+    c.x = __fmaf_rn(x.x, w, c.x);
+    c.y = __fmaf_rn(x.y, w, c.y);
+    c.z = __fmaf_rn(x.z, w, c.z);
+    c.w = __fmaf_rn(x.w, w, c.w);
+  };
   float4 acc[kPer];
 #pragma unroll
   for (int k = 0; k < kPer; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-  const float4* o = reinterpret_cast<const float4*>(a.ws_o + blk0 * NQ * kD);
-  constexpr int kSplit4 = NQ * kD / 4;  // float4 per split
-  int s2 = 0;
-  auto fma4 = [](float4& c, const float4& v, float w) {
-    c.x = __fmaf_rn(v.x, w, c.x);
-    c.y = __fmaf_rn(v.y, w, c.y);
-    c.z = __fmaf_rn(v.z, w, c.z);
-    c.w = __fmaf_rn(v.w, w, c.w);
-  };
-  for (; s2 + kU <= a.splits; s2 += kU) {
-    float4 v[kPer][kU];
+  for (int s2 = 0; s2 < a.splits; s2 += kU) {
+    if (s2 > 0) {
+#pragma unroll
+      for (int k = 0; k < kPer; ++k)
+#pragma unroll
+        for (int u = 0; u < kU; ++u)
+          v[k][u] = s2 + u < a.splits ? __ldcg(o + static_cast<int64_t>(s2 + u) * kSplit4 + tid + k * kThreadsA)
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
 #pragma unroll
     for (int k = 0; k < kPer; ++k)
 #pragma unroll
-      for (int u = 0; u < kU; ++u) v[k][u] = __ldcg(o + static_cast<int64_t>(s2 + u) * kSplit4 + tid + k * kThreadsA);
-#pragma unroll
-    for (int k = 0; k < kPer; ++k)
-#pragma unroll
-      for (int u = 0; u < kU; ++u) fma4(acc[k], v[k][u], w_sm[(s2 + u) * NQ + (tid + k * kThreadsA) / (kD / 4)]);
+      for (int u = 0; u < kU; ++u)
+        if (s2 + u < a.splits) fma4(acc[k], v[k][u], w_sm[(s2 + u) * NQ + (tid + k * kThreadsA) / (kD / 4)]);
   }
-  for (; s2 < a.splits; ++s2)
-#pragma unroll
-    for (int k = 0; k < kPer; ++k)
-      fma4(acc[k], __ldcg(o + static_cast<int64_t>(s2) * kSplit4 + tid + k * kThreadsA),
-           w_sm[s2 * NQ + (tid + k * kThreadsA) / (kD / 4)]);
 #pragma unroll
   for (int k = 0; k < kPer; ++k) {
     const int f = tid + k * kThreadsA;

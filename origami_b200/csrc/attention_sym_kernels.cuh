@@ -164,15 +164,44 @@ __device__ __forceinline__ Win staged_window(const uint32_t* run, uint32_t pos, 
   return r;
 }
 
+// Dims 8 dq .. 8 dq + 7 of a cache row whose element offset without the kv term, `off`,
+// was resolved through the block table when the tile was staged (-1: block id out of
+// range, the row reads as zeros as in cache_row8).
+template <typename QT>
+__device__ __forceinline__ void cache_row8_at(const AttnArgs& a, int kv, int64_t off, int dq, uint32_t (&w)[4]) {
+  if (off < 0) {
+    w[0] = w[1] = w[2] = w[3] = 0u;
+    return;
+  }
+  const int64_t e = kv * a.kv_stride + off + 8 * dq;
+  if (a.cache_vec) {
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(a.cache + e));
+    w[0] = v.x;
+    w[1] = v.y;
+    w[2] = v.z;
+    w[3] = v.w;
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      w[i] = static_cast<uint32_t>(__ldg(a.cache + e + 2 * i)) | (static_cast<uint32_t>(__ldg(a.cache + e + 2 * i + 1)) << 16);
+  }
+  if (a.cache_bf16 != static_cast<int32_t>(is_bf16<QT>())) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      w[i] = pack2<QT>(bits_to_float(static_cast<uint16_t>(w[i] & 0xFFFF), a.cache_bf16 != 0),
+                       bits_to_float(static_cast<uint16_t>(w[i] >> 16), a.cache_bf16 != 0));
+  }
+}
+
 // 8 x 8 block of keys kb.. x dims 8*dq.. in a non-body octet, as rows per key (real
 // values for sink / suffix keys, bias + symbol for body keys, element by element at mixed
 // octets).
 template <typename QT, int CODEC>
 __device__ __forceinline__ void real_rows8(const AttnArgs& a, int kv, int h, int64_t kb, int dq, int64_t kmax,
-                                           float bias, uint32_t (&m)[8][4]) {
+                                           float bias, const int64_t* rowsfx, int64_t k0, uint32_t (&m)[8][4]) {
   if (kb + 7 <= kmax && kb >= a.prefix) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) cache_row8<QT>(a, kv, kb + i, h, dq, m[i]);
+    for (int i = 0; i < 8; ++i) cache_row8_at<QT>(a, kv, rowsfx[kb + i - k0], dq, m[i]);
   } else if (CODEC == 0 && kb + 7 <= kmax && kb + 7 < a.sink) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) sink_row8<QT>(a, kv, kb + i, h, dq, m[i]);
@@ -221,6 +250,29 @@ __device__ __forceinline__ bool named_sync_or_softmax(bool v) {
   return r != 0u;
 }
 
+// First tile of split sp when the nkt tiles are shared by cost: a body tile costs 4, a tile
+// holding sink keys 5 (rows from the sink tensors) and one holding paged-cache keys 7
+// (rows through the block table), in line with their measured times; split sp starts at
+// the tile boundary whose cost(tiles < t) * splits is nearest to sp * cost(all).
+template <int CODEC>
+__device__ __forceinline__ int sym_split_begin(const AttnArgs& a, int sp, int nkt) {
+  if (sp <= 0) return 0;
+  if (sp >= a.splits) return nkt;
+  const int64_t fs = min(static_cast<int64_t>(nkt), a.prefix / kKT);  // first tile with cache keys
+  const int64_t ns = CODEC == 0 ? min(fs, (a.sink + kKT - 1) / kKT) : 0;  // tiles with sink keys before it
+  auto cost = [&](int64_t t) { return 4 * t + min(t, ns) + 3 * max(static_cast<int64_t>(0), t - fs); };
+  const int64_t goal = static_cast<int64_t>(sp) * cost(nkt);
+  int lo = 0, hi = nkt;  // cost(hi) * splits >= goal
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (cost(mid) * a.splits >= goal) hi = mid;
+    else lo = mid + 1;
+  }
+  // the nearer of the two boundaries around the goal (fewer uneven splits than rounding up)
+  if (lo > 0 && goal - cost(lo - 1) * a.splits < cost(lo) * a.splits - goal) --lo;
+  return lo;
+}
+
 // Key range, body range and key groups of tile kt.
 struct SymTile {
   int64_t k0, kend, b_lo, b_hi, g_lo;
@@ -261,7 +313,8 @@ struct AttnSymSmem {
   // cs[4][8]
   static constexpr int n_floats = 4 * 8 + 8 * 8 + 4 * 8 + 4 * 8 + 2 * 8 + 4 * 8;
   static constexpr int cend_off = f_off + n_floats * 4;                        // [8] int64
-  static constexpr int bars_off = cend_off + 8 * 8;                            // 2 mbarriers, TMEM slot, 2 flags
+  static constexpr int rowsfx_off = cend_off + 8 * 8;                          // [128] int64: suffix rows
+  static constexpr int bars_off = rowsfx_off + 128 * 8;                        // 2 mbarriers, TMEM slot, 2 flags
   static constexpr int raw_off = bars_off + 32;
   // staged words: K runs [128][rw] + 2, V runs [128][rw] + 2, key-group rows [3][2][65],
   // per-key value scale / zero [128][2][2]
@@ -297,6 +350,7 @@ __global__ void __launch_bounds__(attn::kThreadsA, 2) prefix_attention_sym(const
   float* zacc = cz + 4 * NQ;      // [2][NQ]: running sum of p * value zero per channel group
   float* cs = zacc + 2 * NQ;      // [4][NQ]: sum of q (.) scale (as rounded) of the tile's key groups
   int64_t* cend = reinterpret_cast<int64_t*>(sm + L::cend_off);
+  int64_t* rowsfx = reinterpret_cast<int64_t*>(sm + L::rowsfx_off);  // the tile's suffix rows, by key - k0
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::bars_off);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 2);
   uint32_t* last_flag = tslot + 1;
@@ -317,8 +371,8 @@ __global__ void __launch_bounds__(attn::kThreadsA, 2) prefix_attention_sym(const
   const int last_row = min(a.rows, row0 + NQ) - 1;
   const int64_t kmax = min(a.seq_len - 1, a.q_start + last_row / a.group);
   const int nkt = static_cast<int>(kmax / kKT) + 1;
-  const int t_begin = static_cast<int>(static_cast<int64_t>(sp) * nkt / a.splits);
-  const int t_end = static_cast<int>(static_cast<int64_t>(sp + 1) * nkt / a.splits);
+  const int t_begin = sym_split_begin<CODEC>(a, sp, nkt);
+  const int t_end = sym_split_begin<CODEC>(a, sp + 1, nkt);
   constexpr bool kBf16 = is_bf16<QT>();
   constexpr uint32_t idesc_s = instr_desc(kBf16, kSymSCols) | (1u << 15);  // MN-major K tile
   constexpr uint32_t idesc_o = CODEC == 0 ? instr_desc(kBf16, kSymOCols) : (instr_desc(kBf16, kSymOCols) | (1u << 15));
@@ -350,6 +404,16 @@ __global__ void __launch_bounds__(attn::kThreadsA, 2) prefix_attention_sym(const
   // bits belong to no body key of the tile.
   auto stage = [&](int kt) {
     const SymTile t = sym_tile<CODEC>(a, kt, kmax);
+    {  // paged-cache keys (at or past the prefix): their rows through the block table
+      const int64_t key = t.k0 + st;
+      if (key >= a.prefix && key <= kmax) {
+        const int64_t bi = key / a.block_size;
+        const int64_t pb = __ldg(a.block_table + bi);
+        rowsfx[st] = (pb < 0 || pb >= a.num_blocks)
+                         ? -1
+                         : pb * a.block_stride + (key - bi * a.block_size) * a.token_stride + static_cast<int64_t>(h) * kD;
+      }
+    }
     if (!t.has_body) return;
     const int64_t koff = CODEC == 0 ? t.k0 - a.sink : t.k0;  // stream token of the tile's key 0
     {  // K runs: dim d starts at bit s_lo * 8 + ((d * H + h) * run + koff) * slot
@@ -548,7 +612,7 @@ __global__ void __launch_bounds__(attn::kThreadsA, 2) prefix_attention_sym(const
       const int64_t kb = k0 + 8 * ko;
       if (ko < ob_lo || ko >= ob_hi) {
         uint32_t m[8][4];
-        real_rows8<QT, CODEC>(a, 0, h, kb, dq, kmax, bias, m);
+        real_rows8<QT, CODEC>(a, 0, h, kb, dq, kmax, bias, rowsfx, k0, m);
         transpose8x8_u16(m);  // rows per dim
 #pragma unroll
         for (int i = 0; i < 8; ++i)
@@ -620,7 +684,7 @@ __global__ void __launch_bounds__(attn::kThreadsA, 2) prefix_attention_sym(const
       const int64_t kb = k0 + 8 * ko;
       if (ko < ob_lo || ko >= ob_hi) {
         uint32_t m[8][4];
-        real_rows8<QT, CODEC>(a, 1, h, kb, dq, kmax, bias, m);  // rows per key
+        real_rows8<QT, CODEC>(a, 1, h, kb, dq, kmax, bias, rowsfx, k0, m);  // rows per key
         if (CODEC == 0) transpose8x8_u16(m);              // K-major V^T: rows per dim
 #pragma unroll
         for (int i = 0; i < 8; ++i)
