@@ -132,7 +132,20 @@ int32_t launch_sym_slot(const origami::AttnArgs& a, int64_t ctas, cudaStream_t s
   int resident = 0;
   int32_t rc = persistent_slots(fn, smem, resident);  // raises the kernel's shared-memory limit
   if (rc) return rc;
-  origami::prefix_attention_sym<QT, CODEC, SLOT><<<static_cast<unsigned>(ctas), origami::attn::kThreadsA, smem, st>>>(a);
+  // programmatic dependent launch: the kernel's setup may overlap the previous kernel's tail
+  // (it waits for that kernel before its first global access)
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(ctas));
+  cfg.blockDim = dim3(origami::attn::kThreadsA);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, origami::prefix_attention_sym<QT, CODEC, SLOT>, a);
+  if (e != cudaSuccess) return cuda_fail(e, "prefix_attention_sym launch");
   return after_launch("prefix_attention_sym launch");
 }
 

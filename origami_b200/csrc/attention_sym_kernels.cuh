@@ -482,6 +482,11 @@ __global__ void __launch_bounds__(attn::kThreadsA, 2) prefix_attention_sym(const
     }
   };
 
+  // Programmatic dependent launch: the next kernel on the stream may start its own setup
+  // now; this one sets up shared memory and TMEM, then waits for the kernels before it
+  // (their results, the workspace they share) before its first global access. Without the
+  // launch attribute both instructions are no-ops.
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
   if (tid == 0) {
     mbar_init(&bars[0], 1);
     mbar_init(&bars[1], 1);
@@ -493,18 +498,27 @@ __global__ void __launch_bounds__(attn::kThreadsA, 2) prefix_attention_sym(const
                  "r"(kSymTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n");
   }
-  if (warp >= 4) {
-    if (t_begin < t_end) stage(t_begin);
-    cp_async_commit();
-  }
-  // byte table, zeroed B blocks of the groups and channel groups, q rows (real block),
-  // per-row causal ends, running sums
+  // byte table, zeroed B blocks of the groups and channel groups, per-row causal ends,
+  // running sums
   if constexpr (kBf16 && SLOT == 8)  // the byte table serves bf16 8-bit symbols only
     lut[tid] = sym_lut_entry<QT>(static_cast<uint32_t>(tid), slot, static_cast<uint32_t>((1 << a.sym_len) - 1));
   for (int e = tid; e < (kSymMaxG * kRowTile) / 16; e += kThreadsA)
     reinterpret_cast<uint4*>(bq_sm)[e] = make_uint4(0u, 0u, 0u, 0u);
   for (int e = tid; e < (kSymMaxC * kRowTile) / 16; e += kThreadsA)
     reinterpret_cast<uint4*>(ps_sm)[e] = make_uint4(0u, 0u, 0u, 0u);
+  if (tid < NQ) {
+    const int row = row0 + tid;
+    m_run[tid] = -INFINITY;
+    l_run[tid] = 0.f;
+    cend[tid] = row < a.rows ? min(a.seq_len - 1, a.q_start + row / a.group) : -1;
+  }
+  if (tid < 10 * NQ) cz[tid] = 0.f;  // cz, zacc, cs
+  asm volatile("griddepcontrol.wait;\n" ::: "memory");
+  // first tile's staged words; q rows (real block)
+  if (warp >= 4) {
+    if (t_begin < t_end) stage(t_begin);
+    cp_async_commit();
+  }
   uint8_t* bq_real = bq_sm + kSymReal * kRowTile;
   if (tid < NQ * 16) {
     const int n = tid >> 4, c = tid & 15;
@@ -520,13 +534,6 @@ __global__ void __launch_bounds__(attn::kThreadsA, 2) prefix_attention_sym(const
     }
     *reinterpret_cast<uint4*>(bq_real + c * kLBO + n * 16) = make_uint4(w[0], w[1], w[2], w[3]);
   }
-  if (tid < NQ) {
-    const int row = row0 + tid;
-    m_run[tid] = -INFINITY;
-    l_run[tid] = 0.f;
-    cend[tid] = row < a.rows ? min(a.seq_len - 1, a.q_start + row / a.group) : -1;
-  }
-  if (tid < 10 * NQ) cz[tid] = 0.f;  // cz, zacc, cs
   __syncthreads();
   // B operands of a key group: threads 0..127 write q (.) scale (one 8-dim chunk c of one
   // row n each), threads 128..255 sum q . zero over the row into cz
