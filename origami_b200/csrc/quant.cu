@@ -59,6 +59,26 @@ int32_t grid_for(const void* fn, int smem, int64_t want, int& grid) {
   return ORIGAMI_OK;
 }
 
+// Launch with programmatic dependent launch: the kernel's CTAs may be scheduled while the
+// kernel before it on the stream finishes; the kernel waits for it (griddepcontrol.wait)
+// before touching global memory.
+template <typename Args>
+int32_t launch_dependent(void (*fn)(Args), int grid, int smem, cudaStream_t st, const Args& a, const char* what) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, fn, a);
+  if (e != cudaSuccess) return cuda_fail(e, what);
+  return after_launch(what);
+}
+
 // ---------------------------------------------------------------------------------------
 template <typename MAXT, typename OUT, bool VEC>
 int32_t launch_cg(const origami::CgArgs& a, cudaStream_t st) {
@@ -66,8 +86,7 @@ int32_t launch_cg(const origami::CgArgs& a, cudaStream_t st) {
   int grid = 0;
   const int32_t rc = grid_for(reinterpret_cast<const void*>(fn), 0, (2 * a.tokens + 7) / 8, grid);
   if (rc) return rc;
-  fn<<<grid, kThreads, 0, st>>>(a);
-  return after_launch("cachegen_to_cache launch");
+  return launch_dependent(fn, grid, 0, st, a, "cachegen_to_cache launch");
 }
 
 template <typename MAXT, typename OUT>
@@ -101,8 +120,7 @@ int32_t launch_kivi_tiles(origami::KiviArgs a, cudaStream_t st) {
   int grid = 0;
   const int32_t rc = grid_for(reinterpret_cast<const void*>(fn), G::smem_bytes, tiles, grid);
   if (rc) return rc;
-  fn<<<grid, kThreads, G::smem_bytes, st>>>(a);
-  return after_launch("kivi_to_cache launch");
+  return launch_dependent(fn, grid, G::smem_bytes, st, a, "kivi_to_cache launch");
 }
 
 template <typename META, typename OUT>

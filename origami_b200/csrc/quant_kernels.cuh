@@ -179,9 +179,17 @@ __device__ __forceinline__ void cg_row_shfl(const uint8_t* s, int64_t nb, int64_
 // element for one symbol value, ((v - c) / c) * max then the output rounding, exactly as the
 // reference does per element, and the other lanes fetch it. Wider symbols go through the
 // shared-memory quotient table, a multiply and a conversion per element.
+// Launched with programmatic dependent launch (the kernel after it may be scheduled early;
+// this one waits for the kernel before it ahead of any global access).
+__device__ __forceinline__ void dependent_launch_entry() {
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+  asm volatile("griddepcontrol.wait;\n" ::: "memory");
+}
+
 template <typename MAXT, typename OUT, bool VEC>
 __global__ void __launch_bounds__(kThreads) cachegen_to_cache(const __grid_constant__ CgArgs a) {
   __shared__ float table[2][256];
+  dependent_launch_entry();
   cg_table(table, a.bins);
   const int lane = threadIdx.x & 31;
   const int64_t rows = 2 * a.tokens;
@@ -423,6 +431,7 @@ __global__ void __launch_bounds__(kThreads) kivi_to_cache(const __grid_constant_
   const int tid = threadIdx.x;
   const int bits = a.bits;
   const int64_t C = static_cast<int64_t>(a.H) * D;
+  dependent_launch_entry();
 
   for (int tile = blockIdx.x; tile < a.num_tiles; tile += gridDim.x) {
     const int tt = tile % a.tiles_per_head;
