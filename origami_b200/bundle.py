@@ -61,8 +61,50 @@ def _bytes_of(t: Any) -> memoryview:
     return memoryview(t)
 
 
-def _numel(t: Any) -> int:
-    return int(t.numel()) if isinstance(t, torch.Tensor) else len(_bytes_of(t))
+class _Slot:
+    """One compressed chunk of a bundle and its place in payload.bin."""
+
+    __slots__ = ("layer", "chunk", "data", "chunk_id", "raw", "size", "offset")
+
+    def __init__(self, layer: str, chunk: ChunkRecord, data: memoryview):
+        self.layer = layer
+        self.chunk = chunk
+        self.data = data
+        self.chunk_id = int(chunk.chunk_id)
+        self.raw = int(chunk.unpacked_bytes)
+        self.size = data.nbytes
+        self.offset = 0
+
+    def chunk_row(self) -> dict[str, Any]:
+        return {
+            "chunk_id": self.chunk_id,
+            "layout": asdict(self.chunk.layout),
+            "codec": str(self.chunk.codec),
+            "compressed_offset": self.offset,
+            "compressed_bytes": self.size,
+            "unpacked_bytes": self.raw,
+        }
+
+
+def _size_groups(run: list[_Slot], with_refs: bool) -> list[dict[str, Any]]:
+    """Rows for the maximal runs of equal unpacked size in `run` (payload.bin order); each
+    row's offset is its first chunk's."""
+    rows: list[dict[str, Any]] = []
+    i = 0
+    while i < len(run):
+        j = i
+        while j < len(run) and run[j].raw == run[i].raw:
+            j += 1
+        part = run[i:j]
+        row: dict[str, Any] = {"output_bytes": run[i].raw, "chunk_ids": [sl.chunk_id for sl in part]}
+        if with_refs:
+            row["refs"] = [{"layer_name": sl.layer, "chunk_id": sl.chunk_id} for sl in part]
+        row["lengths"] = [sl.size for sl in part]
+        row["compressed_offset"] = run[i].offset
+        row["compressed_bytes"] = sum(sl.size for sl in part)
+        rows.append(row)
+        i = j
+    return rows
 
 
 class BundleStore:
@@ -89,90 +131,69 @@ class BundleStore:
 
     # ---------------------------------------------------------------- writing
     def put(self, payload: OrigamiPayload) -> None:
-        """Write `payload` as a bundle_v1 directory (the reference's _put_bundle)."""
-        bundle_dir = self.bundle_dir(payload.cache_key)
-        bundle_dir.mkdir(parents=True, exist_ok=True)
-        layer_chunk_rows: dict[str, dict[int, dict[str, Any]]] = {}
-        layer_group_rows: dict[str, dict[int, dict[str, Any]]] = {}
-        chunks_by_size: dict[int, list[tuple[str, ChunkRecord]]] = {}
-        qat_entries: list[tuple[str, ChunkRecord]] = []
-        for layer_name in sorted(payload.layer_payloads):
-            lp = payload.layer_payloads[layer_name]
-            layer_chunk_rows[layer_name] = {}
-            layer_group_rows[layer_name] = {}
-            for chunk in sorted(lp.chunks, key=lambda c: int(c.chunk_id)):
-                qat_entries.append((layer_name, chunk))
-                chunks_by_size.setdefault(int(chunk.unpacked_bytes), []).append((layer_name, chunk))
-        create_qat = all(codec_uses_qat_bundle(c.codec) for _, c in qat_entries)
-        ordered_groups = sorted(chunks_by_size.items())
-        qat_records = [(int(c.unpacked_bytes), _numel(c.compressed)) for _, c in qat_entries]
-        max_chunk_bytes = max((raw for raw, _ in qat_records), default=1)
+        """Write `payload` as a bundle_v1 directory.
 
-        request_groups = []
-        qat_refs = []
-        qat_path = self.qat_bundle_path(payload.cache_key)
-        if create_qat:
-            with qat_path.open("wb") as qh:
-                qh.write(MAGIC)
-                qh.write(struct.pack("<IIQ", int(max_chunk_bytes), len(qat_records),
-                                     sum(raw for raw, _ in qat_records)))
-                for raw, comp in qat_records:
-                    qh.write(struct.pack("<II", int(raw), int(comp)))
-                for layer_name, chunk in qat_entries:
-                    qh.write(_bytes_of(chunk.compressed))
-                    qat_refs.append({"layer_name": layer_name, "chunk_id": int(chunk.chunk_id),
-                                     "output_bytes": int(chunk.unpacked_bytes)})
-        elif qat_path.exists():
-            qat_path.unlink()
-        with self.payload_path(payload.cache_key).open("wb") as handle:
-            offset = 0
-            for output_bytes, entries in ordered_groups:
-                group_offset = offset
-                lengths, refs = [], []
-                for layer_name, chunk in entries:
-                    data = _bytes_of(chunk.compressed)
-                    handle.write(data)
-                    n = data.nbytes
-                    chunk_id = int(chunk.chunk_id)
-                    lengths.append(n)
-                    refs.append({"layer_name": layer_name, "chunk_id": chunk_id})
-                    layer_chunk_rows[layer_name][chunk_id] = {
-                        "chunk_id": chunk_id,
-                        "layout": asdict(chunk.layout),
-                        "codec": str(chunk.codec),
-                        "compressed_offset": offset,
-                        "compressed_bytes": n,
-                        "unpacked_bytes": int(chunk.unpacked_bytes),
-                    }
-                    group = layer_group_rows[layer_name].setdefault(int(output_bytes), {
-                        "output_bytes": int(output_bytes),
-                        "chunk_ids": [],
-                        "lengths": [],
-                        "compressed_offset": offset,
-                        "compressed_bytes": 0,
-                    })
-                    group["chunk_ids"].append(chunk_id)
-                    group["lengths"].append(n)
-                    group["compressed_bytes"] += n
-                    offset += n
-                request_groups.append({
-                    "output_bytes": int(output_bytes),
-                    "chunk_ids": [int(r["chunk_id"]) for r in refs],
-                    "refs": refs,
-                    "lengths": lengths,
-                    "compressed_offset": group_offset,
-                    "compressed_bytes": sum(lengths),
-                })
+        The bundle is fixed by the format, in three steps:
+
+        1. Canonical chunk order: layers by name, chunks of a layer by id.
+        2. ``payload.bin`` holds the compressed chunks sorted by unpacked size, ascending;
+           chunks of equal size keep the canonical order (so one layer's chunks of a size
+           are adjacent). A chunk's offset is the sum of the sizes before it.
+        3. ``qat_bundle.dz`` (only when every chunk is a raw-deflate stream) holds the
+           ORIGQZ1 header, the (unpacked, compressed) size table and the chunks, all in
+           canonical order.
+
+        The manifest (key order fixed, ``json.dump(..., ensure_ascii=False, indent=2)``)
+        describes both files: per layer its chunk rows (by id) and one row per unpacked
+        size present in the layer; per size over all layers a request group; and the
+        ORIGQZ1 summary with one reference per chunk in canonical order.
+        """
+        folder = self.bundle_dir(payload.cache_key)
+        folder.mkdir(parents=True, exist_ok=True)
+        slots = [_Slot(name, ch, _bytes_of(ch.compressed))
+                 for name in sorted(payload.layer_payloads)
+                 for ch in sorted(payload.layer_payloads[name].chunks, key=lambda c: int(c.chunk_id))]
+        stream = sorted(slots, key=lambda sl: sl.raw)  # stable: equal sizes stay canonical
+        cursor = 0
+        for sl in stream:
+            sl.offset = cursor
+            cursor += sl.size
+        with self.payload_path(payload.cache_key).open("wb") as fh:
+            for sl in stream:
+                fh.write(sl.data)
+
+        deflate = all(codec_uses_qat_bundle(sl.chunk.codec) for sl in slots)
+        qat_file = self.qat_bundle_path(payload.cache_key)
+        qat_summary: dict[str, Any] = {}
+        if deflate:
+            widest = max((sl.raw for sl in slots), default=1)
+            table = b"".join(struct.pack("<II", sl.raw, sl.size) for sl in slots)
+            with qat_file.open("wb") as fh:
+                fh.write(MAGIC + struct.pack("<IIQ", widest, len(slots), sum(sl.raw for sl in slots)) + table)
+                for sl in slots:
+                    fh.write(sl.data)
+            qat_summary = {
+                "format": "ORIGQZ1",
+                "path": qat_file.name,
+                "chunk_bytes": widest,
+                "chunks": len(slots),
+                "compressed_bytes": sum(sl.size for sl in slots),
+                "unpacked_bytes": sum(sl.raw for sl in slots),
+                "refs": [{"layer_name": sl.layer, "chunk_id": sl.chunk_id, "output_bytes": sl.raw} for sl in slots],
+            }
+        elif qat_file.exists():
+            qat_file.unlink()
+
         layers = []
-        for layer_name in sorted(payload.layer_payloads):
-            lp = payload.layer_payloads[layer_name]
-            rows = layer_chunk_rows[layer_name]
+        for name in sorted(payload.layer_payloads):
+            lp = payload.layer_payloads[name]
+            mine = [sl for sl in slots if sl.layer == name]
             layers.append({
                 "layer_name": lp.layer_name,
                 "quantizer": lp.quantizer,
                 "quant_metadata": lp.quant_metadata,
-                "chunks": [rows[i] for i in sorted(rows)],
-                "groups": [layer_group_rows[layer_name][b] for b in sorted(layer_group_rows[layer_name])],
+                "chunks": [sl.chunk_row() for sl in mine],
+                "groups": _size_groups([sl for sl in stream if sl.layer == name], with_refs=False),
             })
         manifest = {
             "format": "bundle_v1",
@@ -184,16 +205,8 @@ class BundleStore:
             "token_count": int(payload.token_count),
             "metadata": dict(payload.metadata),
             "layers": layers,
-            "request_groups": request_groups,
-            "qat_bundle": ({
-                "format": "ORIGQZ1",
-                "path": "qat_bundle.dz",
-                "chunk_bytes": max_chunk_bytes,
-                "chunks": len(qat_records),
-                "compressed_bytes": sum(comp for _, comp in qat_records),
-                "unpacked_bytes": sum(raw for raw, _ in qat_records),
-                "refs": qat_refs,
-            } if create_qat else {}),
+            "request_groups": _size_groups(stream, with_refs=True),
+            "qat_bundle": qat_summary,
         }
         with self.manifest_path(payload.cache_key).open("w", encoding="utf-8") as handle:
             json.dump(manifest, handle, ensure_ascii=False, indent=2, default=str)
