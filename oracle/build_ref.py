@@ -8,6 +8,7 @@ reference kernel itself as a parity pin. Nothing is copied into this repository;
 built module stays out of git (oracle/_ref/ is ignored) and travels to the GPU box.
 
 Usage: python oracle/build_ref.py [reference_root]
+The checkout is the argument, else $ORIGAMI_REFERENCE_ROOT; without either nothing is built.
 """
 from __future__ import annotations
 
@@ -20,7 +21,15 @@ OUT = HERE / "_ref"
 MODULE = "origami_ref_bitpack"
 
 
-def build(reference_root: str = "/root/reference") -> Path | None:
+def reference_root() -> str | None:
+    """The reference checkout named by $ORIGAMI_REFERENCE_ROOT, or None."""
+    return os.environ.get("ORIGAMI_REFERENCE_ROOT") or None
+
+
+def build(reference_root: str | None = None) -> Path | None:
+    reference_root = reference_root or globals()["reference_root"]()
+    if not reference_root:
+        return None
     src = Path(reference_root) / "csrc" / "origami"
     sources = [src / "bitpack_layout_cuda.cpp", src / "bitpack_layout_cuda.cu"]
     if not all(p.exists() for p in sources):
@@ -42,6 +51,6 @@ def build(reference_root: str = "/root/reference") -> Path | None:
 
 
 if __name__ == "__main__":
-    root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    root = sys.argv[1] if len(sys.argv) > 1 else reference_root()
     path = build(root)
     print(path if path else "reference sources not found; oracle/_ref not built")

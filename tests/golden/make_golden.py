@@ -211,4 +211,7 @@ def bundle_cases(m, root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("ORIGAMI_REFERENCE_ROOT")
+    if not root:
+        sys.exit("usage: make_golden.py REFERENCE_ROOT (or set ORIGAMI_REFERENCE_ROOT)")
+    main(root)
