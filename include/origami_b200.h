@@ -160,6 +160,17 @@ int32_t origami_restore_layer_to_paged(
     const int64_t* d_block_ids, int64_t num_block_ids, int64_t num_tokens,
     uint32_t* d_error_count, origami_stream_t stream);
 
+/* Prefix restore: the first restore_tokens (1..num_tokens) tokens of a num_tokens-token
+ * packed layer go to the cache; the other token rows are left as they are, and only the
+ * first ceil(restore_tokens / block_size) block ids are read. Replaces the reference's
+ * partial restore, which narrows the dequantized layer to the request's token count and
+ * copies that many tokens' blocks (worker.py:116-130, 1133-1139, 1165). */
+int32_t origami_restore_layer_prefix_to_paged(
+    const uint8_t* d_packed, int64_t packed_bytes, const origami_planes* planes,
+    const origami_chunk_table* table, const origami_paged_kv* cache,
+    const int64_t* d_block_ids, int64_t num_block_ids, int64_t num_tokens, int64_t restore_tokens,
+    uint32_t* d_error_count, origami_stream_t stream);
+
 /* One job of a batched layer op: a layer (or a request) whose packed bytes start at
  * d_packed + j * job_stride and whose rows live in d_kv_cache (the shared geometry). */
 typedef struct origami_layer_job {

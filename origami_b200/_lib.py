@@ -82,6 +82,9 @@ def _declare(L: ctypes.CDLL) -> None:
     L.origami_pack_layer_from_paged.restype = i32
     L.origami_restore_layer_to_paged.argtypes = [_vp, i64, P(Planes), P(ChunkTable), P(PagedKV), _vp, i64, i64, _vp, _vp]
     L.origami_restore_layer_to_paged.restype = i32
+    L.origami_restore_layer_prefix_to_paged.argtypes = [_vp, i64, P(Planes), P(ChunkTable), P(PagedKV), _vp, i64,
+                                                        i64, i64, _vp, _vp]
+    L.origami_restore_layer_prefix_to_paged.restype = i32
     L.origami_restore_layers_to_paged.argtypes = [_vp, i64, i64, P(Planes), P(ChunkTable), P(PagedKV), P(LayerJob),
                                                   i32, i64, _vp, _vp]
     L.origami_restore_layers_to_paged.restype = i32
@@ -155,6 +158,7 @@ EXPORTS = (
     "origami_pack_canonical_storage_chunks",
     "origami_pack_layer_from_paged",
     "origami_restore_layer_to_paged",
+    "origami_restore_layer_prefix_to_paged",
     "origami_restore_layers_to_paged",
     "origami_pack_layers_from_paged",
     "origami_gather_blocks",

@@ -16,6 +16,7 @@
 #include "tile_kernels.cuh"
 #include "tma_kernels.cuh"
 #include "bulk_kernels.cuh"
+#include "row_kernels.cuh"
 #include "host_common.h"
 
 namespace origami_host {
@@ -356,6 +357,7 @@ int32_t canonical_common(bool restore, const uint8_t* d_packed, int64_t packed_b
     a.H = static_cast<int32_t>(H);
     a.D = static_cast<int32_t>(D);
     a.T = T;
+    a.write_tokens = T;  // canonical symbols: every token
     a.TT = tile_tokens(D);
     a.tiles_per_head = static_cast<int32_t>((T + a.TT - 1) / a.TT);
     a.P = 1;
@@ -435,7 +437,7 @@ struct Job {
 
 template <int MODE, int D>
 int32_t launch_tma(bool restore, const origami_paged_kv* cache, const PagedGeom& g, const Job* jobs, int num_jobs,
-                   int64_t T, const int64_t* off, int64_t S, uint8_t* packed, int64_t job_stride, uint32_t* d_err,
+                   int64_t T, int64_t write_tokens, const int64_t* off, int64_t S, uint8_t* packed, int64_t job_stride, uint32_t* d_err,
                    cudaStream_t st) {
   using G = origami::TmaGeo<MODE, D>;
   auto encode = tensor_map_encoder();
@@ -476,6 +478,7 @@ int32_t launch_tma(bool restore, const origami_paged_kv* cache, const PagedGeom&
     a.block_size = cache->block_size;
     a.num_blocks = cache->num_blocks;
     a.T = T;
+    a.write_tokens = write_tokens;
     a.H = static_cast<int32_t>(cache->num_heads);
     a.tiles_per_head = tiles_per_head;
     const int64_t tiles = tiles_per_job * nj;
@@ -494,12 +497,12 @@ int32_t launch_tma(bool restore, const origami_paged_kv* cache, const PagedGeom&
 
 template <int MODE>
 int32_t launch_tma_by_dim(bool restore, int64_t D, const origami_paged_kv* cache, const PagedGeom& g, const Job* jobs,
-                          int num_jobs, int64_t T, const int64_t* off, int64_t S, uint8_t* packed, int64_t job_stride,
+                          int num_jobs, int64_t T, int64_t write_tokens, const int64_t* off, int64_t S, uint8_t* packed, int64_t job_stride,
                           uint32_t* err, cudaStream_t st) {
   switch (D) {
-    case 64: return launch_tma<MODE, 64>(restore, cache, g, jobs, num_jobs, T, off, S, packed, job_stride, err, st);
-    case 128: return launch_tma<MODE, 128>(restore, cache, g, jobs, num_jobs, T, off, S, packed, job_stride, err, st);
-    default: return launch_tma<MODE, 256>(restore, cache, g, jobs, num_jobs, T, off, S, packed, job_stride, err, st);
+    case 64: return launch_tma<MODE, 64>(restore, cache, g, jobs, num_jobs, T, write_tokens, off, S, packed, job_stride, err, st);
+    case 128: return launch_tma<MODE, 128>(restore, cache, g, jobs, num_jobs, T, write_tokens, off, S, packed, job_stride, err, st);
+    default: return launch_tma<MODE, 256>(restore, cache, g, jobs, num_jobs, T, write_tokens, off, S, packed, job_stride, err, st);
   }
 }
 
@@ -524,7 +527,7 @@ bool bulk_eligible(int mode, const std::vector<Spec>& specs, const int64_t* off,
 
 template <int MODE, int D>
 int32_t launch_bulk(bool restore, const origami_paged_kv* cache, const PagedGeom& g, const Job* jobs, int num_jobs,
-                    int64_t T, const int64_t* off, int64_t S, uint8_t* packed, int64_t packed_bytes, int64_t job_stride,
+                    int64_t T, int64_t write_tokens, const int64_t* off, int64_t S, uint8_t* packed, int64_t packed_bytes, int64_t job_stride,
                     uint32_t* d_err, cudaStream_t st) {
   using G = origami::TmaGeo<MODE, D>;
   const void* fn = restore ? reinterpret_cast<const void*>(&origami::restore_bulk<MODE, D>)
@@ -553,6 +556,7 @@ int32_t launch_bulk(bool restore, const origami_paged_kv* cache, const PagedGeom
     a.block_size = cache->block_size;
     a.num_blocks = cache->num_blocks;
     a.T = T;
+    a.write_tokens = write_tokens;
     a.H = static_cast<int32_t>(cache->num_heads);
     a.tiles_per_head = tiles_per_head;
     const int64_t tiles = tiles_per_job * nj;
@@ -571,24 +575,133 @@ int32_t launch_bulk(bool restore, const origami_paged_kv* cache, const PagedGeom
 
 template <int MODE>
 int32_t launch_bulk_by_dim(bool restore, int64_t D, const origami_paged_kv* cache, const PagedGeom& g, const Job* jobs,
-                           int num_jobs, int64_t T, const int64_t* off, int64_t S, uint8_t* packed,
+                           int num_jobs, int64_t T, int64_t write_tokens, const int64_t* off, int64_t S, uint8_t* packed,
                            int64_t packed_bytes, int64_t job_stride, uint32_t* err, cudaStream_t st) {
   switch (D) {
     case 64:
-      return launch_bulk<MODE, 64>(restore, cache, g, jobs, num_jobs, T, off, S, packed, packed_bytes, job_stride, err, st);
+      return launch_bulk<MODE, 64>(restore, cache, g, jobs, num_jobs, T, write_tokens, off, S, packed, packed_bytes, job_stride, err, st);
     case 128:
-      return launch_bulk<MODE, 128>(restore, cache, g, jobs, num_jobs, T, off, S, packed, packed_bytes, job_stride, err,
+      return launch_bulk<MODE, 128>(restore, cache, g, jobs, num_jobs, T, write_tokens, off, S, packed, packed_bytes, job_stride, err,
                                     st);
     default:
-      return launch_bulk<MODE, 256>(restore, cache, g, jobs, num_jobs, T, off, S, packed, packed_bytes, job_stride, err,
+      return launch_bulk<MODE, 256>(restore, cache, g, jobs, num_jobs, T, write_tokens, off, S, packed, packed_bytes, job_stride, err,
                                     st);
+  }
+}
+
+// Row kernels (row_kernels.cuh) for head_dim 128 and 256: restore for every plane preset,
+// aligned (TMA) or ragged (bulk copies) runs; pack for byte planes.
+template <int MODE, int D>
+int32_t launch_rows(bool restore, bool ragged, const origami_paged_kv* cache, const PagedGeom& g, const Job* jobs,
+                    int num_jobs, int64_t T, int64_t write_tokens, const int64_t* off, int64_t S, uint8_t* packed, int64_t packed_bytes,
+                    int64_t job_stride, uint32_t* d_err, cudaStream_t st) {
+  using G = origami::TmaGeo<MODE, D>;
+  const void* fn;
+  int smem;
+  if (restore && ragged) {
+    fn = reinterpret_cast<const void*>(&origami::restore_rows<MODE, D, true>);
+    smem = origami::RestoreRowsGeo<MODE, D, true>::smem_bytes;
+  } else if (restore) {
+    fn = reinterpret_cast<const void*>(&origami::restore_rows<MODE, D, false>);
+    smem = origami::RestoreRowsGeo<MODE, D, false>::smem_bytes;
+  } else {
+    fn = reinterpret_cast<const void*>(&origami::pack_rows<D>);
+    smem = origami::PackRowsGeo<D>::smem_bytes;
+  }
+  const bool maps = restore && !ragged;
+  auto encode = maps ? tensor_map_encoder() : nullptr;
+  if (maps && encode == nullptr) return fail(ORIGAMI_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  int resident = 0;
+  int32_t rc = persistent_slots(fn, smem, resident);
+  if (rc) return rc;
+  const int P = G::P;
+  // pack tiles own PackRowsGeo::STEP tokens each (their windows overlap by LOOK tokens)
+  const int64_t tile_step = restore ? G::TT : origami::PackRowsGeo<D>::STEP;
+  const int32_t tiles_per_head = static_cast<int32_t>((T + tile_step - 1) / tile_step);
+  const int64_t tiles_per_job = 2 * cache->num_heads * tiles_per_head;
+  for (int j0 = 0; j0 < num_jobs; j0 += origami::kMaxJobs) {
+    const int nj = std::min(num_jobs - j0, origami::kMaxJobs);
+    origami::RowArgs a{};
+    a.packed = packed + static_cast<int64_t>(j0) * job_stride;
+    a.job_stride = job_stride;
+    a.packed_bytes = packed_bytes - static_cast<int64_t>(j0) * job_stride;
+    for (int q = 0; q < 2 * P; ++q) a.comp_base[q] = off[q * S];
+    for (int p = 0; p < P; ++p) a.run_bytes[p] = T * G::bits(p) / 8;
+    if (maps) {
+      for (int q = 0; q < 2 * P; ++q) {
+        const int b = G::bits(q % P);
+        const cuuint64_t dims[3] = {static_cast<cuuint64_t>(T * b / 8), static_cast<cuuint64_t>(cache->num_heads * D),
+                                    static_cast<cuuint64_t>(nj)};
+        const cuuint64_t strides[2] = {static_cast<cuuint64_t>(T * b / 8), static_cast<cuuint64_t>(job_stride)};
+        const cuuint32_t box[3] = {static_cast<cuuint32_t>(G::TT * b / 8), static_cast<cuuint32_t>(D), 1};
+        const cuuint32_t estr[3] = {1, 1, 1};
+        const CUresult r = encode(&a.maps[q], CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, a.packed + off[q * S], dims, strides,
+                                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                  CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) return fail(ORIGAMI_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+      }
+    }
+    for (int j = 0; j < nj; ++j) {
+      a.rows[j] = jobs[j0 + j].rows;
+      a.block_ids[j] = jobs[j0 + j].ids;
+    }
+    a.kv_stride = g.kv_stride;
+    a.block_stride = g.block_stride;
+    a.token_stride = g.token_stride;
+    a.head_stride = g.head_stride;
+    a.block_size = cache->block_size;
+    a.num_blocks = cache->num_blocks;
+    a.T = T;
+    a.write_tokens = write_tokens;
+    a.H = static_cast<int32_t>(cache->num_heads);
+    a.tiles_per_head = tiles_per_head;
+    const int64_t tiles = tiles_per_job * nj;
+    if (tiles > 0x7FFFFFFF) return fail(ORIGAMI_ERR_UNSUPPORTED, "too many tiles");
+    a.tiles_per_job = static_cast<int32_t>(tiles_per_job);
+    a.num_tiles = static_cast<int32_t>(tiles);
+    a.err = d_err;
+    const int grid = static_cast<int>(std::min<int64_t>(tiles, resident));
+    if (restore && ragged) origami::restore_rows<MODE, D, true><<<grid, kThreads, smem, st>>>(a);
+    else if (restore) origami::restore_rows<MODE, D, false><<<grid, kThreads, smem, st>>>(a);
+    else origami::pack_rows<D><<<grid, kThreads, smem, st>>>(a);
+    rc = after_launch(restore ? "restore_rows launch" : "pack_rows launch");
+    if (rc) return rc;
+  }
+  return ORIGAMI_OK;
+}
+
+template <int MODE>
+int32_t launch_rows_by_dim(bool restore, bool ragged, int64_t D, const origami_paged_kv* cache, const PagedGeom& g,
+                           const Job* jobs, int num_jobs, int64_t T, int64_t write_tokens, const int64_t* off, int64_t S, uint8_t* packed,
+                           int64_t packed_bytes, int64_t job_stride, uint32_t* err, cudaStream_t st) {
+  if (D == 128)
+    return launch_rows<MODE, 128>(restore, ragged, cache, g, jobs, num_jobs, T, write_tokens, off, S, packed, packed_bytes, job_stride,
+                                  err, st);
+  return launch_rows<MODE, 256>(restore, ragged, cache, g, jobs, num_jobs, T, write_tokens, off, S, packed, packed_bytes, job_stride,
+                                err, st);
+}
+
+int32_t launch_rows_by_mode(int mode, bool restore, bool ragged, int64_t D, const origami_paged_kv* cache,
+                            const PagedGeom& g, const Job* jobs, int num_jobs, int64_t T, int64_t write_tokens,
+                            const int64_t* off, int64_t S,
+                            uint8_t* packed, int64_t packed_bytes, int64_t job_stride, uint32_t* err, cudaStream_t st) {
+  switch (mode) {
+    case origami::kModeByte2:
+      return launch_rows_by_dim<origami::kModeByte2>(restore, ragged, D, cache, g, jobs, num_jobs, T, write_tokens, off, S, packed,
+                                                     packed_bytes, job_stride, err, st);
+    case origami::kModeBf16Bits:
+      return launch_rows_by_dim<origami::kModeBf16Bits>(restore, ragged, D, cache, g, jobs, num_jobs, T, write_tokens, off, S,
+                                                        packed, packed_bytes, job_stride, err, st);
+    default:
+      return launch_rows_by_dim<origami::kModeFp16Bits>(restore, ragged, D, cache, g, jobs, num_jobs, T, write_tokens, off, S,
+                                                        packed, packed_bytes, job_stride, err, st);
   }
 }
 
 // Fused layer ops over `num_jobs` jobs sharing one chunk table and cache geometry; job j's
 // packed bytes start at d_packed + j * job_stride.
 int32_t layer_common(bool restore, const origami_paged_kv* cache, const Job* jobs, int num_jobs, int64_t T,
-                     const origami_planes* planes, const origami_chunk_table* table, uint8_t* d_packed,
+                     int64_t write_tokens, const origami_planes* planes, const origami_chunk_table* table, uint8_t* d_packed,
                      int64_t packed_bytes, int64_t job_stride, uint32_t* d_err, cudaStream_t st) {
   if (cache == nullptr) return fail(ORIGAMI_ERR_INVALID, "kv cache descriptor is null");
   if (num_jobs <= 0 || jobs == nullptr) return fail(ORIGAMI_ERR_INVALID, "at least one job is required");
@@ -606,7 +719,9 @@ int32_t layer_common(bool restore, const origami_paged_kv* cache, const Job* job
   if (T <= 0) return fail(ORIGAMI_ERR_INVALID, "num_tokens must be positive");
   if (T > 0x7FFFFFFF || cache->block_size > 0x7FFFFFFF)
     return fail(ORIGAMI_ERR_UNSUPPORTED, "num_tokens and block_size must be below 2^31");
-  const int64_t need_blocks = (T + cache->block_size - 1) / cache->block_size;
+  if (write_tokens <= 0 || write_tokens > T)
+    return fail(ORIGAMI_ERR_INVALID, "restore_tokens must be in [1, num_tokens]");
+  const int64_t need_blocks = (write_tokens + cache->block_size - 1) / cache->block_size;
   for (int j = 0; j < num_jobs; ++j) {
     if (jobs[j].rows == nullptr || !aligned(jobs[j].rows, 16))
       return fail(ORIGAMI_ERR_INVALID, "job %d: kv cache must be non-null and 16-byte aligned", j);
@@ -646,29 +761,36 @@ int32_t layer_common(bool restore, const origami_paged_kv* cache, const Job* job
   if (num_jobs == 1) job_stride = (off[nchunks] + 15) & ~static_cast<int64_t>(15);
 
   const int mode = classify_planes(*planes);
-  if (tma_eligible(mode, specs, off, planes, T, H, D, d_packed)) {
+  // restore_rows for every preset at head_dim 128 / 256; pack_rows for ragged byte planes
+  // there (aligned byte planes pack faster through pack_tma's staged TMA stores)
+  const bool aligned_runs = tma_eligible(mode, specs, off, planes, T, H, D, d_packed);
+  const bool rows = (D == 128 || D == 256) && (restore || (mode == origami::kModeByte2 && !aligned_runs));
+  if (rows && (aligned_runs || bulk_eligible(mode, specs, off, planes, T, D, d_packed, num_jobs, job_stride)))
+    return launch_rows_by_mode(mode, restore, !aligned_runs, D, &geom, g, jobs, num_jobs, T, write_tokens, off, S, d_packed,
+                               packed_bytes, job_stride, d_err, st);
+  if (aligned_runs) {
     switch (mode) {
       case origami::kModeByte2:
-        return launch_tma_by_dim<origami::kModeByte2>(restore, D, &geom, g, jobs, num_jobs, T, off, S, d_packed,
+        return launch_tma_by_dim<origami::kModeByte2>(restore, D, &geom, g, jobs, num_jobs, T, write_tokens, off, S, d_packed,
                                                       job_stride, d_err, st);
       case origami::kModeBf16Bits:
-        return launch_tma_by_dim<origami::kModeBf16Bits>(restore, D, &geom, g, jobs, num_jobs, T, off, S, d_packed,
+        return launch_tma_by_dim<origami::kModeBf16Bits>(restore, D, &geom, g, jobs, num_jobs, T, write_tokens, off, S, d_packed,
                                                          job_stride, d_err, st);
       default:
-        return launch_tma_by_dim<origami::kModeFp16Bits>(restore, D, &geom, g, jobs, num_jobs, T, off, S, d_packed,
+        return launch_tma_by_dim<origami::kModeFp16Bits>(restore, D, &geom, g, jobs, num_jobs, T, write_tokens, off, S, d_packed,
                                                          job_stride, d_err, st);
     }
   }
   if (bulk_eligible(mode, specs, off, planes, T, D, d_packed, num_jobs, job_stride)) {
     switch (mode) {
       case origami::kModeByte2:
-        return launch_bulk_by_dim<origami::kModeByte2>(restore, D, &geom, g, jobs, num_jobs, T, off, S, d_packed,
+        return launch_bulk_by_dim<origami::kModeByte2>(restore, D, &geom, g, jobs, num_jobs, T, write_tokens, off, S, d_packed,
                                                        packed_bytes, job_stride, d_err, st);
       case origami::kModeBf16Bits:
-        return launch_bulk_by_dim<origami::kModeBf16Bits>(restore, D, &geom, g, jobs, num_jobs, T, off, S, d_packed,
+        return launch_bulk_by_dim<origami::kModeBf16Bits>(restore, D, &geom, g, jobs, num_jobs, T, write_tokens, off, S, d_packed,
                                                           packed_bytes, job_stride, d_err, st);
       default:
-        return launch_bulk_by_dim<origami::kModeFp16Bits>(restore, D, &geom, g, jobs, num_jobs, T, off, S, d_packed,
+        return launch_bulk_by_dim<origami::kModeFp16Bits>(restore, D, &geom, g, jobs, num_jobs, T, write_tokens, off, S, d_packed,
                                                           packed_bytes, job_stride, d_err, st);
     }
   }
@@ -688,6 +810,7 @@ int32_t layer_common(bool restore, const origami_paged_kv* cache, const Job* job
   a.H = static_cast<int32_t>(H);
   a.D = static_cast<int32_t>(D);
   a.T = T;
+  a.write_tokens = write_tokens;
   a.TT = tile_tokens(D);
   a.tiles_per_head = static_cast<int32_t>((T + a.TT - 1) / a.TT);
   a.P = P;
@@ -776,8 +899,8 @@ int32_t origami_pack_layer_from_paged(const origami_paged_kv* cache, const int64
                                       uint32_t* d_error_count, origami_stream_t stream) {
   if (cache == nullptr) return fail(ORIGAMI_ERR_INVALID, "kv cache is null");
   const Job job{cache->d_data, d_block_ids, num_block_ids};
-  return layer_common(false, cache, &job, 1, num_tokens, planes, table, d_packed, packed_bytes, 0, d_error_count,
-                      reinterpret_cast<cudaStream_t>(stream));
+  return layer_common(false, cache, &job, 1, num_tokens, num_tokens, planes, table, d_packed, packed_bytes, 0,
+                      d_error_count, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int32_t origami_restore_layer_to_paged(const uint8_t* d_packed, int64_t packed_bytes, const origami_planes* planes,
@@ -786,8 +909,19 @@ int32_t origami_restore_layer_to_paged(const uint8_t* d_packed, int64_t packed_b
                                        uint32_t* d_error_count, origami_stream_t stream) {
   if (cache == nullptr) return fail(ORIGAMI_ERR_INVALID, "kv cache is null");
   const Job job{cache->d_data, d_block_ids, num_block_ids};
-  return layer_common(true, cache, &job, 1, num_tokens, planes, table, const_cast<uint8_t*>(d_packed), packed_bytes,
-                      0, d_error_count, reinterpret_cast<cudaStream_t>(stream));
+  return layer_common(true, cache, &job, 1, num_tokens, num_tokens, planes, table, const_cast<uint8_t*>(d_packed),
+                      packed_bytes, 0, d_error_count, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int32_t origami_restore_layer_prefix_to_paged(const uint8_t* d_packed, int64_t packed_bytes,
+                                              const origami_planes* planes, const origami_chunk_table* table,
+                                              const origami_paged_kv* cache, const int64_t* d_block_ids,
+                                              int64_t num_block_ids, int64_t num_tokens, int64_t restore_tokens,
+                                              uint32_t* d_error_count, origami_stream_t stream) {
+  if (cache == nullptr) return fail(ORIGAMI_ERR_INVALID, "kv cache is null");
+  const Job job{cache->d_data, d_block_ids, num_block_ids};
+  return layer_common(true, cache, &job, 1, num_tokens, restore_tokens, planes, table, const_cast<uint8_t*>(d_packed),
+                      packed_bytes, 0, d_error_count, reinterpret_cast<cudaStream_t>(stream));
 }
 
 static int32_t jobs_from(const origami_layer_job* jobs, int32_t n, std::vector<Job>& out) {
@@ -804,7 +938,7 @@ int32_t origami_pack_layers_from_paged(const origami_paged_kv* cache, const orig
   std::vector<Job> js;
   const int32_t rc = jobs_from(jobs, num_jobs, js);
   if (rc) return rc;
-  return layer_common(false, cache, js.data(), num_jobs, num_tokens, planes, table, d_packed, packed_bytes,
+  return layer_common(false, cache, js.data(), num_jobs, num_tokens, num_tokens, planes, table, d_packed, packed_bytes,
                       job_stride, d_error_count, reinterpret_cast<cudaStream_t>(stream));
 }
 
@@ -816,8 +950,9 @@ int32_t origami_restore_layers_to_paged(const uint8_t* d_packed, int64_t packed_
   std::vector<Job> js;
   const int32_t rc = jobs_from(jobs, num_jobs, js);
   if (rc) return rc;
-  return layer_common(true, cache, js.data(), num_jobs, num_tokens, planes, table, const_cast<uint8_t*>(d_packed),
-                      packed_bytes, job_stride, d_error_count, reinterpret_cast<cudaStream_t>(stream));
+  return layer_common(true, cache, js.data(), num_jobs, num_tokens, num_tokens, planes, table,
+                      const_cast<uint8_t*>(d_packed), packed_bytes, job_stride, d_error_count,
+                      reinterpret_cast<cudaStream_t>(stream));
 }
 
 int32_t origami_gather_blocks(const origami_paged_kv* cache, const int64_t* d_block_ids, int64_t num_block_ids,

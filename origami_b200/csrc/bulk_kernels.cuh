@@ -31,6 +31,7 @@ struct BulkArgs {
   int64_t kv_stride, block_stride, token_stride, head_stride;
   int64_t block_size, num_blocks;
   int64_t T;
+  int64_t write_tokens;  // restore: token rows below this are written (a prefix restore when < T)
   int32_t H, tiles_per_head, tiles_per_job, num_tiles;
   uint32_t* err;
 };

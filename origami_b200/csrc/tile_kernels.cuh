@@ -56,6 +56,7 @@ struct TileArgs {
   // Geometry.
   int32_t num_kv, H, D;
   int64_t T;
+  int64_t write_tokens;  // restore: token rows below this are written (a prefix restore when < T)
   int32_t TT, tiles_per_head;
   // Planes (bits[p] is the widest chunk's width when chunk_bits is set).
   int32_t P;
@@ -147,6 +148,10 @@ __device__ __forceinline__ void tile_setup(const TileArgs& args, const TileCoord
   const int32_t bs = static_cast<int32_t>(args.block_size);
   for (int t = threadIdx.x; t < tc.n; t += kThreads) {
     const int32_t tg = static_cast<int32_t>(tc.t0) + t;
+    if (tg >= args.write_tokens) {
+      rowoff[t] = -1;
+      continue;
+    }
     const int32_t bi = tg / bs;
     const int64_t blk = args.block_ids ? args.block_ids[bi] : bi;
     if (blk < 0 || blk >= args.num_blocks) {

@@ -37,6 +37,7 @@ struct TmaArgs {
   int64_t kv_stride, block_stride, token_stride, head_stride;
   int64_t block_size, num_blocks;
   int64_t T;
+  int64_t write_tokens;  // restore: token rows below this are written (a prefix restore when < T)
   int32_t H, tiles_per_head, tiles_per_job, num_tiles;
   uint32_t* err;
 };
@@ -123,7 +124,7 @@ __device__ __forceinline__ void rowoff_load(const Args& a, const Tile& t, Rowoff
   for (int k = 0; k < RowoffRegs<TT>::kPer; ++k) {
     const int i = static_cast<int>(threadIdx.x) + k * kThreads;
     int64_t off = -1;
-    if (i < TT && i < t.n) {
+    if (i < TT && i < t.n && t.t0 + i < a.write_tokens) {
       const int32_t tg = static_cast<int32_t>(t.t0) + i;
       const int32_t bi = tg / bs;
       const int64_t blk = a.block_ids[t.job][bi];

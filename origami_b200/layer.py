@@ -106,8 +106,10 @@ def pack_layer(kv_layer: torch.Tensor, block_ids, fmt: LayerFormat, *, out: torc
 
 
 def restore_layer(packed: torch.Tensor, fmt: LayerFormat, kv_layer: torch.Tensor, block_ids, *,
-                  stream: torch.cuda.Stream | None = None, error_count: torch.Tensor | None = None) -> None:
-    """Restore tokens [0, fmt.num_tokens) of a request into the paged cache."""
+                  stream: torch.cuda.Stream | None = None, error_count: torch.Tensor | None = None,
+                  num_tokens: int | None = None) -> None:
+    """Restore tokens [0, fmt.num_tokens) of a request into the paged cache, or only the
+    first `num_tokens` of them (a prefix restore: later token rows are left as they are)."""
     device = kv_layer.device
     desc = paged_desc(kv_layer)
     if desc.num_heads != fmt.num_heads or desc.head_dim != fmt.head_dim:
@@ -117,12 +119,19 @@ def restore_layer(packed: torch.Tensor, fmt: LayerFormat, kv_layer: torch.Tensor
     ids = block_ids_tensor(block_ids, device)
     pl = planes_desc(fmt)
     tab = _table(fmt, device)
+    err = error_count.data_ptr() if error_count is not None else None
     with torch.cuda.device(device):
-        rc = _lib.lib().origami_restore_layer_to_paged(
-            packed.data_ptr(), packed.numel(), ctypes.byref(pl), ctypes.byref(tab), ctypes.byref(desc),
-            ids.data_ptr(), ids.numel(), fmt.num_tokens, error_count.data_ptr() if error_count is not None else None,
-            _stream_handle(stream, device))
-    _lib.check(rc, "origami_restore_layer_to_paged")
+        if num_tokens is None or int(num_tokens) == fmt.num_tokens:
+            rc = _lib.lib().origami_restore_layer_to_paged(
+                packed.data_ptr(), packed.numel(), ctypes.byref(pl), ctypes.byref(tab), ctypes.byref(desc),
+                ids.data_ptr(), ids.numel(), fmt.num_tokens, err, _stream_handle(stream, device))
+            what = "origami_restore_layer_to_paged"
+        else:
+            rc = _lib.lib().origami_restore_layer_prefix_to_paged(
+                packed.data_ptr(), packed.numel(), ctypes.byref(pl), ctypes.byref(tab), ctypes.byref(desc),
+                ids.data_ptr(), ids.numel(), fmt.num_tokens, int(num_tokens), err, _stream_handle(stream, device))
+            what = "origami_restore_layer_prefix_to_paged"
+    _lib.check(rc, what)
 
 
 def _jobs(kv_layers, block_ids, device) -> tuple[_lib.PagedKV, ctypes.Array, list]:
@@ -222,16 +231,21 @@ def scatter_blocks(value: torch.Tensor, kv_layer: torch.Tensor, block_ids, *,
 
 def fused_kernel_name(fmt: LayerFormat, restore: bool = True) -> str:
     """Name of the kernel the fused op launches for this format (the dispatch rules of
-    csrc/abi.cu: TMA tensor-map kernels for 16-byte aligned runs, bulk-copy kernels for
-    byte-aligned contiguous runs, generic tile kernels otherwise; the packed buffer is
-    assumed 16-byte aligned)."""
+    csrc/abi.cu, the packed buffer assumed 16-byte aligned): for the plane presets with
+    contiguous runs, the row kernels at head_dim 128 / 256 (restore for every preset, pack
+    for byte planes with ragged runs), else TMA tensor-map kernels for 16-byte aligned runs and bulk-copy
+    kernels for byte-aligned runs; generic tile kernels otherwise."""
     presets = {(8, 0): (8, 8), (7, 15, 0): (8, 1, 7), (10, 8, 0): (6, 2, 8)}
     D, T = fmt.head_dim, fmt.num_tokens
     tt = 8 * (2048 // D)
     preset = presets.get(tuple(fmt.planes.shifts)) == tuple(fmt.planes.bits) and D in (64, 128, 256)
-    if preset and all((T * b) % 128 == 0 and (tt * b) % 128 == 0 for b in fmt.planes.bits):
+    aligned = preset and all((T * b) % 128 == 0 and (tt * b) % 128 == 0 for b in fmt.planes.bits)
+    ragged = preset and not aligned and all((T * b) % 8 == 0 for b in fmt.planes.bits)
+    if (aligned or ragged) and D in (128, 256) and (restore or (ragged and tuple(fmt.planes.bits) == (8, 8))):
+        return "restore_rows" if restore else "pack_rows"
+    if aligned:
         return "restore_tma" if restore else "pack_tma"
-    if preset and all((T * b) % 8 == 0 for b in fmt.planes.bits):
+    if ragged:
         return "restore_bulk" if restore else "pack_bulk"
     return "restore_tiles" if restore else "pack_tiles"
 

@@ -181,3 +181,41 @@ def test_batched_jobs_match_per_job(oracle, cuda, planes, T, jobs):
         blk = ids[j][t // bs]
         assert torch.equal(fresh[j].cpu()[:, blk, t % bs].view(torch.int16),
                            caches[j].cpu()[:, blk, t % bs].view(torch.int16)), j
+
+
+@pytest.mark.parametrize("planes", [BYTE_PLANES, BF16_BIT_PLANES, ODD_PLANES], ids=lambda p: p.name)
+@pytest.mark.parametrize("geom", [(1000, 16, 8, 128, 613), (4096, 16, 2, 128, 4000), (333, 32, 4, 256, 33),
+                                  (2048, 32, 4, 64, 1500), (30000, 16, 8, 128, 29999)],
+                         ids=lambda g: "T%d_bs%d_H%d_D%d_to%d" % g)
+def test_prefix_restore_writes_only_the_first_tokens(oracle, cuda, geom, planes):
+    """A restore of the first T' < T tokens (the reference narrows a restored layer to
+    the request's token count, worker.py:116-130, 1165): rows of those tokens equal a full
+    restore's, every other row of the cache keeps its bytes, and only the first
+    ceil(T' / block_size) block ids are read."""
+    T, bs, H, D, Tp = geom
+    cache, ids = make_cache(T, bs, H, D, True, seed=T + 3)
+    fmt = LayerFormat(T, H, D, planes)
+    want, _ = oracle.pack_layer(u16(cache), 0, ids.numpy(), T, planes.shifts, planes.bits, fmt.specs)
+    dst, _ = make_cache(T, bs, H, D, True, seed=T + 4)
+    full = u16(dst).copy()
+    oracle.restore_layer(want, planes.shifts, planes.bits, fmt.specs, full, 0, ids.numpy(), T)
+    expect = u16(dst).copy()
+    t = np.arange(Tp)
+    blk = ids.numpy()[t // bs]
+    expect[:, blk, t % bs] = full[:, blk, t % bs]
+    d_dst = dst.to(cuda)
+    need = (Tp + bs - 1) // bs
+    short_ids = ids[:need].clone()
+    restore_layer(torch.from_numpy(want).to(cuda), fmt, d_dst, short_ids.to(cuda), num_tokens=Tp)
+    np.testing.assert_array_equal(u16(d_dst.cpu()), expect)
+
+
+def test_prefix_restore_checks_its_token_count(cuda):
+    T, bs, H, D = 256, 16, 2, 128
+    cache, ids = make_cache(T, bs, H, D, True, seed=9)
+    fmt = LayerFormat(T, H, D, BYTE_PLANES)
+    d = cache.to(cuda)
+    packed = pack_layer(d, ids, fmt)
+    for bad in (0, T + 1):
+        with pytest.raises(RuntimeError, match="restore_tokens"):
+            restore_layer(packed, fmt, d, ids, num_tokens=bad)
