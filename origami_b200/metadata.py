@@ -5,6 +5,8 @@ reference's origami package), so payloads written by either side stay interchang
 """
 from __future__ import annotations
 
+import sys
+
 from dataclasses import dataclass, field
 from typing import Any
 
@@ -77,9 +79,26 @@ class OrigamiSaveRequest:
     token_start: int = 0
 
 
+_ConnectorMetadataBase: type = object
+if "vllm" in sys.modules:  # inside a vLLM process: derive from its connector metadata base
+    try:
+        from vllm.distributed.kv_transfer.kv_connector.v1.base import KVConnectorMetadata as _ConnectorMetadataBase
+    except Exception:  # noqa: BLE001
+        _ConnectorMetadataBase = object
+
+
 @dataclass
-class OrigamiConnectorMetadata:
-    """What the scheduler side hands the worker each step (metadata.py:74-92)."""
+class OrigamiConnectorMetadata(_ConnectorMetadataBase):
+    """What the scheduler side hands the worker each step (metadata.py:74-92): the
+    requests to restore / save, the GPU lossless share, and the fused-attention requests
+    with their query positions, counts, batch indices, codecs and prefix lengths."""
 
     reqs_to_restore: dict[str, OrigamiRestoreRequest] = field(default_factory=dict)
     reqs_to_save: dict[str, OrigamiSaveRequest] = field(default_factory=dict)
+    gpu_lossless_ratio: int = 0
+    fused_request_ids: tuple[str, ...] = ()
+    fused_query_start_positions: dict[str, int] = field(default_factory=dict)
+    fused_query_token_counts: dict[str, int] = field(default_factory=dict)
+    fused_request_indices: dict[str, int] = field(default_factory=dict)
+    fused_codecs: dict[str, str] = field(default_factory=dict)
+    fused_prefix_lengths: dict[str, int] = field(default_factory=dict)

@@ -26,7 +26,8 @@ from dataclasses import dataclass
 
 import torch
 
-from origami_b200.layer import pack_layer, restore_layer
+from origami_b200 import _lib
+from origami_b200.layer import cache_layout, pack_layer, restore_layer, scatter_blocks
 from origami_b200.planes import LayerFormat
 
 
@@ -49,13 +50,12 @@ class RestorePipeline:
         self._next = 0
         self.launches = 0
 
-    def enqueue(self, host_packed: torch.Tensor, fmt: LayerFormat, kv_layer: torch.Tensor, block_ids,
-                error_count: torch.Tensor | None = None) -> torch.cuda.Event:
-        """Queue one layer; returns the event that marks the layer as restored."""
-        if host_packed.device.type != "cpu" or not host_packed.is_pinned():
+    def _upload(self, host: torch.Tensor, n: int) -> _Slot:
+        """Copy n pinned bytes into the next ring slot on the copy stream; the restore
+        stream waits for that copy only."""
+        if host.device.type != "cpu" or not host.is_pinned():
             raise ValueError("host packed layer must be in pinned host memory")
-        n = fmt.packed_bytes
-        if host_packed.numel() < n:
+        if host.numel() < n:
             raise ValueError("host packed layer is shorter than the layer format")
         slot = self.slots[self._next]
         self._next = (self._next + 1) % len(self.slots)
@@ -64,16 +64,42 @@ class RestorePipeline:
         if slot.used:
             self.copy_stream.wait_event(slot.free)  # previous user of the slot has been unpacked
         with torch.cuda.stream(self.copy_stream):
-            slot.buf[:n].copy_(host_packed[:n], non_blocking=True)
+            slot.buf[:n].copy_(host[:n], non_blocking=True)
             slot.copied.record(self.copy_stream)
         self.restore_stream.wait_event(slot.copied)
-        restore_layer(slot.buf[:n], fmt, kv_layer, block_ids, stream=self.restore_stream, error_count=error_count)
+        return slot
+
+    def _done(self, slot: _Slot) -> torch.cuda.Event:
         self.launches += 1
         slot.free.record(self.restore_stream)
         slot.used = True
         ready = torch.cuda.Event()
         ready.record(self.restore_stream)
         return ready
+
+    def enqueue(self, host_packed: torch.Tensor, fmt: LayerFormat, kv_layer: torch.Tensor, block_ids,
+                error_count: torch.Tensor | None = None, *, num_tokens: int | None = None) -> torch.cuda.Event:
+        """Queue one layer (or its first num_tokens tokens); returns the event that marks
+        the layer as restored."""
+        n = fmt.packed_bytes
+        slot = self._upload(host_packed, n)
+        restore_layer(slot.buf[:n], fmt, kv_layer, block_ids, stream=self.restore_stream, error_count=error_count,
+                      num_tokens=num_tokens)
+        return self._done(slot)
+
+    def enqueue_raw(self, host_bytes: torch.Tensor, nbytes: int, shape, kv_layer: torch.Tensor, block_ids,
+                    num_blocks: int, error_count: torch.Tensor | None = None) -> torch.cuda.Event:
+        """Queue one raw-bytes layer (the gathered [2, n, bs, H, D] or [n, 2, bs, H, D]
+        blocks): copy it into a ring slot and scatter its first num_blocks blocks into the
+        cache by block table."""
+        slot = self._upload(host_bytes, nbytes)
+        value = slot.buf[:nbytes].view(kv_layer.dtype).view(list(shape))
+        block_dim = 1 if cache_layout(kv_layer) == _lib.ORIGAMI_KV_FIRST else 0
+        with torch.cuda.stream(self.restore_stream):
+            if num_blocks < value.shape[block_dim]:
+                value = value.narrow(block_dim, 0, num_blocks).contiguous()
+            scatter_blocks(value, kv_layer, block_ids, stream=self.restore_stream, error_count=error_count)
+        return self._done(slot)
 
     def enqueue_from_bundle(self, bundle, layer_name: str, fmt: LayerFormat, kv_layer: torch.Tensor, block_ids,
                             error_count: torch.Tensor | None = None, *, threads: int = 0) -> torch.cuda.Event:

@@ -13,9 +13,9 @@ start_load_kv  : per request, a host thread decompresses each layer's chunks dir
                  into a pinned staging buffer (no cat, no pageable copy) and enqueues it
                  on the RestorePipeline (copy stream -> ring slot -> restore kernel ->
                  per-layer event).
-wait_for_layer_load : the future of each pending request for that layer yields its
-                 event; the model's current stream waits on it (no host block beyond
-                 the codec's progress).
+wait_for_layer_load : each pending request's layer event is published when the
+                 layer is enqueued; the model's current stream waits on it (a host wait
+                 only while the codec has not yet decoded that layer).
 
 Layout policies: 'byte' / 'bit' (plane format origami_planes_v1) and 'raw' (the
 reference's raw-bytes layout: gathered blocks in 1 MiB chunks, RawBytesTensorAdapter
@@ -33,7 +33,7 @@ from typing import Any
 import numpy as np
 import torch
 
-from origami_b200.layer import gather_blocks, pack_layer, raw_chunk_bounds, scatter_blocks
+from origami_b200.layer import gather_blocks, raw_chunk_bounds
 from origami_b200.metadata import (ChunkLayout, ChunkRecord, LayerPayload, OrigamiConnectorMetadata, OrigamiPayload,
                                    OrigamiRestoreRequest, OrigamiSaveRequest)
 from origami_b200.pipeline import RestorePipeline, SavePipeline
@@ -136,6 +136,7 @@ class OrigamiB200Worker:
         self._restore_futures: dict[Future, str] = {}
         self._save_futures: list[Future] = []
         self._save_payloads: dict[str, OrigamiPayload] = {}
+        self.host_waits = 0  # wait_for_layer_load calls that found a layer still being decoded
 
     # ------------------------------------------------------------------ setup
     def register_kv_caches(self, kv_caches: dict[str, torch.Tensor]) -> None:
@@ -303,6 +304,11 @@ class OrigamiB200Worker:
 
     # ------------------------------------------------------------------ restore
     def start_load_kv(self, metadata: OrigamiConnectorMetadata) -> None:
+        """Queue every layer of every request to restore. A request thread decodes layer
+        after layer into pinned staging (its chunks in parallel on the codec pool) and
+        enqueues each on the restore pipeline as soon as it is decoded, so layer L + 1
+        decodes while layer L is copied and restored; the layer's event is published the
+        moment it is enqueued."""
         self._metadata = metadata
         for restore in metadata.reqs_to_restore.values():
             futs: dict[str, Future] = {}
@@ -318,11 +324,12 @@ class OrigamiB200Worker:
         try:
             payload = self.store.get(restore.cache_key)
             ids_list = [int(b) for b in (restore.block_ids_per_group[0] if restore.block_ids_per_group else ())]
+            ids_dev = torch.tensor(ids_list, dtype=torch.int64, device=self.device) if ids_list else None
             for layer_name, fut in futs.items():
                 if fut.done():
                     continue
                 try:
-                    fut.set_result(self._restore_layer(payload, restore, layer_name, ids_list))
+                    fut.set_result(self._restore_layer(payload, restore, layer_name, ids_list, ids_dev))
                 except Exception as exc:  # noqa: BLE001
                     fut.set_exception(exc)
                     raise
@@ -334,42 +341,38 @@ class OrigamiB200Worker:
             raise
 
     def _restore_layer(self, payload: OrigamiPayload, restore: OrigamiRestoreRequest, layer_name: str,
-                       ids_list: list[int]) -> torch.cuda.Event | None:
+                       ids_list: list[int], ids_dev: torch.Tensor | None) -> torch.cuda.Event | None:
         lp = payload.layer_payloads.get(layer_name)
         if lp is None:
             return None
         kv_cache = self.kv_caches[layer_name]
+        bs, H, D = self._geometry(kv_cache)
         native = lp.quant_metadata.get(NATIVE_LAYOUT_KEY) or {}
         fmt_name = str(lp.quant_metadata.get("format"))
+        want = int(restore.num_tokens)
         if fmt_name == "raw_bytes":
             nb = int(lp.quant_metadata["num_blocks"])
             nbytes = int(lp.quant_metadata["byte_count"])
-            ids = torch.tensor(ids_list[:nb], dtype=torch.int64)
-            if len(ids) != nb:
+            if len(ids_list) < nb:
                 raise RuntimeError("Origami restore request has fewer blocks than the artifact")
+            # a shorter request restores the whole blocks its tokens need (worker.py:1133-1139)
+            use = min(nb, (want + bs - 1) // bs) if want > 0 else nb
             host = self._pinned.take(nbytes)
             data = host.numpy()
             bounds = [0] + [int(s[3]) for s in native["chunk_specs"]]
             list(self._codec_pool.map(lambda k: self._decompress_into(lp.chunks[k].compressed,
                                                                       data[bounds[k]:bounds[k + 1]]),
                                       range(len(lp.chunks))))
-            side = self._raw_side_stream()
-            with torch.cuda.stream(side):
-                dev = torch.empty((nbytes,), dtype=torch.uint8, device=self.device)
-                dev.copy_(host[:nbytes], non_blocking=True)
-                value = dev.view(kv_cache.dtype).view(lp.quant_metadata["shape"])
-                scatter_blocks(value, kv_cache, ids.pin_memory().to(self.device, non_blocking=True), stream=side)
-                ev = torch.cuda.Event()
-                ev.record(side)
+            restore_pipe, _ = self._pipes(nbytes)
+            with self._pipe_lock:
+                ev = restore_pipe.enqueue_raw(host, nbytes, lp.quant_metadata["shape"], kv_cache, ids_dev[:use], use)
             self._pinned.release_after(host, ev)
             return ev
         if fmt_name != FORMAT_NAME:
             raise RuntimeError(f"unsupported Origami payload format {fmt_name!r}")
         T = int(native["token_count"])
-        if int(restore.num_tokens) != T:
-            raise RuntimeError(f"Origami restore of {restore.num_tokens} tokens from a {T}-token artifact "
-                               "(partial plane-format restores are not supported)")
-        bs, H, D = self._geometry(kv_cache)
+        if want <= 0 or want > T:
+            want = T
         if int(native["num_heads"]) != H or int(native["head_dim"]) != D:
             raise RuntimeError("artifact heads / head_dim do not match the KV cache")
         planes = plane_spec(native["planes"], kv_cache.dtype)
@@ -377,10 +380,9 @@ class OrigamiB200Worker:
         fmt = LayerFormat(T, H, D, planes, *chunk_sizes)
         if fmt.specs.tolist() != native["chunk_specs"] or len(lp.chunks) != fmt.num_chunks:
             raise RuntimeError("Origami native layout metadata chunk count does not match payload chunks")
-        need = (T + bs - 1) // bs
+        need = (want + bs - 1) // bs
         if len(ids_list) < need:
             raise RuntimeError("Origami restore request has fewer blocks than its tokens need")
-        ids = torch.tensor(ids_list[:need], dtype=torch.int64).pin_memory().to(self.device, non_blocking=True)
         host = self._pinned.take(fmt.packed_bytes)
         data = host.numpy()
         offs = fmt.offsets
@@ -388,15 +390,22 @@ class OrigamiB200Worker:
                                   range(fmt.num_chunks)))
         restore_pipe, _ = self._pipes(fmt.packed_bytes)
         with self._pipe_lock:
-            ev = restore_pipe.enqueue(host, fmt, kv_cache, ids)
+            ev = restore_pipe.enqueue(host, fmt, kv_cache, ids_dev[:need], num_tokens=want)
         self._pinned.release_after(host, ev)
         return ev
 
     def wait_for_layer_load(self, layer_name: str) -> None:
+        """Order the model's current stream after this layer's restore. A layer that is
+        already enqueued costs one stream->event wait and no host wait; only a layer whose
+        chunks are still being decoded makes the caller wait for the codec (the reference
+        waits on the layer's future every time, worker.py:553-572)."""
+        stream = torch.cuda.current_stream(self.device)
         for fut in self._pending_layer_futures.pop(layer_name, []):
+            if not fut.done():
+                self.host_waits += 1
             ev = fut.result()
             if ev is not None:
-                torch.cuda.current_stream(self.device).wait_event(ev)
+                stream.wait_event(ev)
 
     def get_finished(self, finished_req_ids: set[str] | None = None) -> tuple[set[str], set[str]]:
         del finished_req_ids

@@ -5,7 +5,7 @@ import numpy as np
 import pytest
 import torch
 
-from origami_b200 import workloads
+from origami_b200 import BYTE_PLANES, LayerFormat, workloads
 from origami_b200.metadata import OrigamiConnectorMetadata, OrigamiRestoreRequest, OrigamiSaveRequest
 from origami_b200.worker import InMemoryStore, OrigamiB200Worker
 
@@ -75,3 +75,90 @@ def test_missing_artifact_surfaces_in_wait(cuda):
     with pytest.raises(KeyError):
         w.wait_for_layer_load("layer.0")
     w.shutdown()
+
+
+@pytest.mark.parametrize("policy", ["byte", "bit", "raw"])
+def test_partial_restore_through_hooks(cuda, policy):
+    """Save T tokens, restore T' < T through the hooks: the T' token rows come back
+    byte-exact and rows past them keep their bytes (whole blocks for the raw layout,
+    which restores the blocks the T' tokens need, as the reference does)."""
+    T, Tp, bs, H, D, layers = 1000, 613, 16, 4, 128, 2
+    nb = (T + bs - 1) // bs
+    NB = nb + 7
+    ids = workloads.permuted_block_table(nb, NB, seed=23)
+    caches, values = _caches(cuda, layers, T, bs, H, D, NB, ids, seed=60)
+    store = InMemoryStore()
+    kw = dict(layout_policy=policy, chunk_min_bytes=1 << 16, chunk_target_bytes=1 << 16, chunk_max_bytes=1 << 16,
+              store=store, device=cuda)
+    w = OrigamiB200Worker(**kw)
+    w.register_kv_caches(caches)
+    ids_t = tuple(int(i) for i in ids)
+    w.start_load_kv(OrigamiConnectorMetadata(reqs_to_save={"r0": OrigamiSaveRequest("r0", "k", (ids_t,), T)}))
+    for name, c in caches.items():
+        w.save_kv_layer(name, c, None)
+    w.wait_for_save()
+
+    sentinel = {n: torch.full_like(c, 3.0) for n, c in caches.items()}
+    fresh = {n: c.clone() for n, c in sentinel.items()}
+    w2 = OrigamiB200Worker(**kw)
+    w2.register_kv_caches(fresh)
+    w2.start_load_kv(OrigamiConnectorMetadata(reqs_to_restore={"r1": OrigamiRestoreRequest("r1", "k", (ids_t,), Tp)}))
+    for name in fresh:
+        w2.wait_for_layer_load(name)
+    torch.cuda.synchronize()
+    upto = (Tp + bs - 1) // bs * bs if policy == "raw" else Tp
+    t = torch.arange(upto)
+    for name, c in fresh.items():
+        got = c.cpu()
+        assert torch.equal(got[:, ids[t // bs], t % bs].view(torch.int16), values[name][:, :upto].view(torch.int16))
+        untouched = got.clone()
+        untouched[:, ids[t // bs], t % bs] = sentinel[name].cpu()[:, ids[t // bs], t % bs]
+        assert torch.equal(untouched.view(torch.int16), sentinel[name].cpu().view(torch.int16)), name
+    w.shutdown()
+    w2.shutdown()
+
+
+def test_wait_for_layer_load_is_a_stream_wait_once_enqueued(cuda):
+    """Once a layer is enqueued, wait_for_layer_load costs the forward thread no host
+    wait: it returns while the layer's restore is still running on the GPU and only
+    orders the current stream after it."""
+    T, bs, H, D, layers = 4096, 16, 8, 128, 3
+    nb = T // bs
+    ids = workloads.permuted_block_table(nb, nb, seed=5)
+    caches, values = _caches(cuda, layers, T, bs, H, D, nb, ids, seed=70)
+    store = InMemoryStore()
+    kw = dict(layout_policy="byte", store=store, device=cuda, lossless_backend="raw")
+    w = OrigamiB200Worker(**kw)
+    w.register_kv_caches(caches)
+    ids_t = tuple(int(i) for i in ids)
+    w.start_load_kv(OrigamiConnectorMetadata(reqs_to_save={"r0": OrigamiSaveRequest("r0", "k", (ids_t,), T)}))
+    for name, c in caches.items():
+        w.save_kv_layer(name, c, None)
+    w.wait_for_save()
+
+    fresh = {n: torch.zeros_like(c) for n, c in caches.items()}
+    w2 = OrigamiB200Worker(**kw)
+    w2.register_kv_caches(fresh)
+    # hold the restore pipeline's streams behind a long device sleep, so that the restore
+    # events are certainly still pending when the forward thread asks for the layers
+    restore_pipe, _ = w2._pipes(LayerFormat(T, H, D, BYTE_PLANES).packed_bytes)
+    with torch.cuda.stream(restore_pipe.copy_stream):
+        torch.cuda._sleep(200_000_000)
+    w2.start_load_kv(OrigamiConnectorMetadata(reqs_to_restore={"r1": OrigamiRestoreRequest("r1", "k", (ids_t,), T)}))
+    futs = [f for fl in w2._pending_layer_futures.values() for f in fl]
+    for f in futs:
+        f.result(timeout=60)  # every layer decoded and enqueued
+    events = [f.result() for f in futs]
+    for name in fresh:
+        w2.wait_for_layer_load(name)
+    assert w2.host_waits == 0
+    assert not all(ev.query() for ev in events)  # returned while the restores were still queued
+    done = torch.cuda.Event()
+    done.record(torch.cuda.current_stream(cuda))
+    done.synchronize()  # the current stream was ordered after every layer's restore
+    assert all(ev.query() for ev in events)
+    t = torch.arange(T)
+    for name, c in fresh.items():
+        assert torch.equal(c.cpu()[:, ids[t // bs], t % bs].view(torch.int16), values[name].view(torch.int16))
+    w.shutdown()
+    w2.shutdown()
