@@ -46,7 +46,8 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("origami", "reference"), default="origami")
     ap.add_argument("--planes", default="byte", help="byte | bit | bf16_bits | fp16_bits")
-    ap.add_argument("--layers", type=int, default=0, help="layers (default: 32 for C2, 4 for C3, 8 for C5)")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="layers (default: 32 for C2, as many of 32 as fit one GPU for C3, 8 for C5)")
     ap.add_argument("--config", choices=("C2", "C3", "C5", "CG", "KIVI", "ATTN"), default="C2",
                     help="workload (C2 is the headline; CG / KIVI: quantized restore paths)")
     ap.add_argument("--chunk-bytes", type=int, default=1 << 20, help="codec chunk size (min = target = max)")
@@ -101,6 +102,10 @@ def max_over_ranks(x: float, world: int, device=None) -> float:
     t = torch.tensor([x], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def min_over_ranks(x: float, world: int, device=None) -> float:
+    return -max_over_ranks(-x, world, device)
 
 
 def any_over_ranks(flag: bool, world: int, device=None) -> bool:
@@ -271,6 +276,9 @@ class Workload:
             for j, (layer, r) in enumerate(jobs):
                 self.packed[layer][r] = arena[j * stride:j * stride + fmt.packed_bytes]
             self.groups.append((fmt, jobs, arena))
+        # C3's pool is most of the GPU: instead of a copy of every cache, a restore is checked
+        # by packing the restored cache again (pack o restore = identity on the request rows)
+        self.keep_orig = config != "C3"
         self.caches, self.orig = [], []
         for layer in range(layers):
             cache = torch.zeros((2, self.NB, self.bs, self.heads, cfg.head_dim), dtype=cfg.dtype, device=device)
@@ -280,7 +288,8 @@ class Workload:
                                          device=device)[:, :, self.head0:self.head0 + self.heads]
                 workloads.scatter_into_cache(cache, kv.contiguous(), self.block_ids[r])
                 pack_layer(cache, self.block_ids[r], self.fmts[r], out=self.packed[layer][r])
-            self.orig.append(cache.clone())
+            if self.keep_orig:
+                self.orig.append(cache.clone())
             self.caches.append(cache)
         torch.cuda.synchronize()
 
@@ -313,7 +322,32 @@ class Workload:
     def verify(self) -> bool:
         import torch
 
-        return all(torch.equal(c.view(torch.int16), o.view(torch.int16)) for c, o in zip(self.caches, self.orig))
+        if self.keep_orig:
+            return all(torch.equal(c.view(torch.int16), o.view(torch.int16)) for c, o in zip(self.caches, self.orig))
+        from origami_b200.layer import pack_layers
+
+        for fmt, jobs, arena in self.groups:
+            again = torch.empty_like(arena)
+            pack_layers([self.caches[layer] for layer, _ in jobs], [self.block_ids[r] for _, r in jobs], fmt, again)
+            if not torch.equal(again, arena):
+                return False
+            del again
+        return True
+
+    @staticmethod
+    def layers_that_fit(config: str, world: int, device) -> int:
+        """C3 at as many of its 32 layers as one GPU holds (pool + packed layers, with room
+        for the verification buffer and temporaries)."""
+        import torch
+
+        from origami_b200 import workloads
+
+        cfg = workloads.c3_config()
+        heads = cfg.heads // world
+        per_token = 2 * heads * cfg.head_dim * 2
+        per_layer = workloads.c3_pool_blocks(cfg) * cfg.block_size * per_token + sum(cfg.tokens) * per_token
+        free, _ = torch.cuda.mem_get_info(device)
+        return max(1, min(32, int((free - 16 * 2**30) // per_layer)))
 
 
 def run_origami(args, rank, world, local):
@@ -322,7 +356,10 @@ def run_origami(args, rank, world, local):
     from origami_b200.layer import fused_kernel_name, pack_layers, restore_layers
 
     device = torch.device("cuda", local)
-    layers = args.layers if args.layers else {"C2": 32, "C3": 4, "C5": 8}[args.config]
+    layers = args.layers if args.layers else {"C2": 32, "C5": 8}.get(args.config) or Workload.layers_that_fit(
+        args.config, world, device)
+    if args.config == "C3" and not args.layers:
+        layers = int(min_over_ranks(layers, world, device))
     wl = Workload(args.config, rank, world, layers, args.planes, device, args.chunk_bytes, args.tokens)
     stream = torch.cuda.current_stream(device)
     err = torch.zeros(1, dtype=torch.int32, device=device)
