@@ -59,6 +59,8 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="bound on the CPU baseline sample")
     ap.add_argument("--no-pipeline", action="store_true", help="skip the C4 exposed-restore measurement")
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="C2: skip the reference's own GPU restore (its unpack kernel + index_copy_)")
     ap.add_argument("--pipeline-layers", type=int, default=8, help="C4 layers sampled by the pipeline measurement")
     return ap.parse_args()
 
@@ -186,16 +188,21 @@ def measured_hbm_peak():
 
 
 def profiled_traffic(kernel: str, workload: str, jobs_per_launch: float):
-    """DRAM read+write bytes per launch: the committed ncu figure per job (one layer of
-    one request; the traffic of a launch grows in proportion to its jobs) times the
-    jobs one launch restores or packs."""
+    """DRAM read+write bytes per launch from the committed ncu captures
+    (profiles/traffic.txt): lines `kernel workload jobs read write` measured on a launch
+    of `jobs` jobs (the bench's own launch where it fits a capture), or older
+    `kernel workload bytes_per_job` lines; scaled to the jobs one launch restores or
+    packs."""
     p = REPO / "profiles" / "traffic.txt"
     if not p.exists():
         return None
     for line in p.read_text().splitlines():
         parts = line.split()
-        if len(parts) >= 3 and parts[0] == kernel and parts[1] == workload:
-            return int(round(int(parts[2]) * jobs_per_launch))
+        if line.startswith("#") or len(parts) < 3 or parts[0] != kernel or parts[1] != workload:
+            continue
+        if len(parts) >= 5:
+            return int(round((int(parts[3]) + int(parts[4])) * jobs_per_launch / int(parts[2])))
+        return int(round(int(parts[2]) * jobs_per_launch))
     return None
 
 
@@ -467,7 +474,7 @@ def run_origami(args, rank, world, local):
     k_pack = "/".join(sorted({fused_kernel_name(f, False) for f in wl.fmts}))
     jobs_per_launch = sum(len(jobs) for _, jobs, _ in wl.groups) / launches
     workload_name = (f"C2_restore_T{wl.tokens[0]}_H{wl.heads}_D{wl.cfg.head_dim}_{wl.planes.name}"
-                     if args.config == "C2" and args.chunk_bytes == 1 << 20 and not args.tokens else None)
+                     if args.config == "C2" and args.chunk_bytes == 1 << 20 else None)
     roof_restore = {"kernel": k_restore, "bound": "hbm", "achieved": round(achieved_restore, 1), "peak": peak,
                     "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved_restore / peak, 4),
                     "traffic": profiled_traffic(k_restore, workload_name, jobs_per_launch) if workload_name else None,
@@ -485,10 +492,19 @@ def run_origami(args, rank, world, local):
         pipeline_info = run_pipeline_c4(args, device, world)
         ok = ok and pipeline_info.pop("ok")
 
+    pcie = measure_pcie(device)
+    if pipeline_info is not None:
+        pipeline_info["pcie_h2d_frac"] = round(pipeline_info["pcie_h2d_gbs"] / pcie["h2d_gbs"], 3)
     e2e = None
     if not args.no_e2e:
         e2e = run_e2e_save(args, wl, device, world) if primary_pack else run_e2e(args, wl, device, world)
         ok = ok and e2e.pop("ok")
+        link = "d2h" if primary_pack else "h2d"
+        if f"pcie_{link}_gbs" in e2e:
+            e2e[f"pcie_{link}_frac"] = round(e2e[f"pcie_{link}_gbs"] / pcie[f"{link}_gbs"], 3)
+    reference_gpu = None
+    if args.config == "C2" and not primary_pack and not args.no_reference_gpu and wl.keep_orig:
+        reference_gpu = run_reference_gpu_restore(args, wl, device)
     bundle_info = None
     if args.bundle_e2e and not primary_pack:
         bundle_info = run_bundle_e2e(args, wl, device, world)
@@ -538,17 +554,108 @@ def run_origami(args, rank, world, local):
         "clocks": clock_info,
         "verified": bool(ok),
     }
+    result["pcie"] = pcie
     if e2e is not None:
         result["e2e"] = e2e
     if pipeline_info is not None:
         result["pipeline"] = pipeline_info
+    if reference_gpu is not None:
+        result["reference_gpu"] = reference_gpu
     if bundle_info is not None:
         result["bundle_e2e"] = bundle_info
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        result["cpu_baseline"] = cpu_baseline(args, wl)
+        result["cpu_baseline"], result["cpu_baselines"] = cpu_baseline(args, wl)
     if rank == 0:
         print(json.dumps(result), flush=True)
     return 0 if ok else 1
+
+
+def measure_pcie(device) -> dict:
+    """Pinned host <-> device copy peak of this box, in this run: 256 MiB cudaMemcpyAsync
+    each way on one stream, best of 10 after 3 warm-ups (the roofline of the e2e and
+    pipeline numbers)."""
+    import torch
+
+    n = 256 << 20
+    host = torch.empty((n,), dtype=torch.uint8, pin_memory=True)
+    dev = torch.empty((n,), dtype=torch.uint8, device=device)
+    stream = torch.cuda.Stream(device)
+    out = {}
+    for name, fn in (("h2d_gbs", lambda: dev.copy_(host, non_blocking=True)),
+                     ("d2h_gbs", lambda: host.copy_(dev, non_blocking=True))):
+        best = float("inf")
+        with torch.cuda.stream(stream):
+            for i in range(13):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                fn()
+                b.record(stream)
+                b.synchronize()
+                if i >= 3:
+                    best = min(best, a.elapsed_time(b))
+        out[name] = round(n / (best / 1e3) / GB, 2)
+    out["how"] = "pinned cudaMemcpyAsync of 256 MiB, best of 10"
+    return out
+
+
+def run_reference_gpu_restore(args, wl, device) -> dict | None:
+    """The reference's own GPU restore of the same layers, inputs resident in HBM: each
+    layer's raw-bytes symbols (the gathered blocks, RawBytesTensorAdapter,
+    quantization/raw_tensor.py:100-122) in 1 MiB chunks go through the reference's
+    unpack_canonical_storage_chunks_cuda (lossless/native_gpu.py:113-146 -> csrc/origami/
+    bitpack_layout_cuda.cpp:316-400 -> .cu:91-128, built from the reference's sources into
+    oracle/_ref), the dequantize view (raw_tensor.py:125-157) and the index_copy_ block
+    scatter of copy_kv_to_hbm (benchmark_utils.py:434-444, 465-532)."""
+    import torch
+
+    sys.path.insert(0, str(REPO / "tests" / "golden"))
+    try:
+        from make_ref_vectors import load_reference_extension
+
+        ext = load_reference_extension()
+    except Exception:  # noqa: BLE001
+        ext = None
+    if ext is None:
+        return None
+    layers = []
+    for layer in range(wl.layers):
+        for r in range(wl.requests):
+            ids = wl.block_ids[r]
+            gathered = torch.index_select(wl.orig[layer], 1, ids)  # the saved layer's blocks
+            flat = gathered.reshape(-1).view(torch.uint8).contiguous()
+            n = flat.numel()
+            bounds = list(range(0, n, 1 << 20)) + [n]
+            specs = torch.tensor([[0, 1, a, b, 0, 1] for a, b in zip(bounds[:-1], bounds[1:])], dtype=torch.int64,
+                                 device=device)
+            layers.append((layer, r, flat, torch.tensor(bounds, dtype=torch.int64, device=device),
+                           torch.full((len(bounds) - 1,), 8, dtype=torch.int64, device=device), specs,
+                           torch.tensor([1, 1, n], dtype=torch.int64), list(gathered.shape)))
+    axes = torch.tensor([0, 1, 2, -1], dtype=torch.int64)
+    for c in wl.caches:
+        c.zero_()
+
+    def step():
+        for layer, r, flat, offs, bits, specs, shape, vshape in layers:
+            out = ext.unpack_canonical_storage_chunks_cuda(flat, offs, bits, shape, axes, 1, 1, int(shape[2]), specs)
+            value = out.view(wl.cfg.dtype).view(vshape)
+            wl.caches[layer].index_copy_(1, wl.block_ids[r], value)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(device)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize(device)
+    ms = t0.elapsed_time(t1)
+    ok = all(torch.equal(c.view(torch.int16), o.view(torch.int16)) for c, o in zip(wl.caches, wl.orig))
+    del layers
+    return {"value": round(wl.kv_bytes_per_step * args.steps / (ms / 1e3) / GB, 1), "unit": "GB/s",
+            "ms_per_step": round(ms / args.steps, 3), "verified": ok,
+            "path": "reference unpack_canonical_storage_chunks_cuda on each layer's raw-bytes chunks (1 MiB, 8 bits) "
+                    "+ dequantize view + index_copy_ block scatter, inputs resident in HBM"}
 
 
 def run_e2e(args, wl, device, world):
@@ -831,15 +938,16 @@ def run_pipeline_c4(args, device, world):
 
 
 def cpu_baseline(args, wl):
-    """The CPU oracle on the host cores over a bounded sample of the config's layers
-    (request 0): restore for C2/C3, pack for C5."""
+    """CPU baselines on the host cores over bounded samples of the config's layers
+    (request 0), each about args.cpu_seconds: the oracle port of the layout (restore; pack
+    for C5) on all host threads (the headline entry) and on one thread, and for restores
+    the reference connector's own CPU lossless restore of the raw-bytes layout (zlib level 1
+    chunks -> cat -> view -> index_copy_, oracle/ref_lossless.py)."""
     import torch
 
     sys.path.insert(0, str(REPO / "oracle"))
     import oracle
 
-    threads = os.cpu_count() or 1
-    oracle.set_threads(threads)
     fmt, T = wl.fmts[0], wl.tokens[0]
     ids = wl.block_ids[0].cpu().numpy()
     pack_dir = args.config == "C5"
@@ -849,21 +957,53 @@ def cpu_baseline(args, wl):
     else:
         packed = [wl.packed[layer][0].cpu().numpy() for layer in range(layers)]
         cache = np.zeros((2, wl.NB, wl.bs, wl.heads, wl.cfg.head_dim), dtype=np.uint16)
-    done = 0
-    t0 = time.perf_counter()
-    while done < layers:
-        if pack_dir:
-            oracle.pack_layer(caches[done], 0, ids, T, wl.planes.shifts, wl.planes.bits, fmt.specs)
-        else:
-            oracle.restore_layer(packed[done], wl.planes.shifts, wl.planes.bits, fmt.specs, cache, 0, ids, T)
-        done += 1
-        if time.perf_counter() - t0 > args.cpu_seconds:
-            break
-    dt = time.perf_counter() - t0
     what = "pack_layer" if pack_dir else "restore_layer"
-    return {"value": round(done * fmt.kv_bytes / dt / GB, 3), "unit": "GB/s", "cores": oracle.max_threads(),
-            "kind": "port", "sample": f"{done} {args.config} layers x 1 request ({done * fmt.kv_bytes / 2**20:.0f} MiB "
-            f"KV), oracle {what}, {dt:.1f} s"}
+
+    def port(threads: int) -> dict:
+        oracle.set_threads(threads)
+        done = 0
+        t0 = time.perf_counter()
+        while done < layers:
+            if pack_dir:
+                oracle.pack_layer(caches[done], 0, ids, T, wl.planes.shifts, wl.planes.bits, fmt.specs)
+            else:
+                oracle.restore_layer(packed[done], wl.planes.shifts, wl.planes.bits, fmt.specs, cache, 0, ids, T)
+            done += 1
+            if time.perf_counter() - t0 > args.cpu_seconds:
+                break
+        dt = time.perf_counter() - t0
+        return {"value": round(done * fmt.kv_bytes / dt / GB, 3), "unit": "GB/s", "cores": oracle.max_threads(),
+                "kind": "port", "sample": f"{done} {args.config} layers x 1 request ({done * fmt.kv_bytes / 2**20:.0f} "
+                f"MiB KV), oracle {what}, {dt:.1f} s"}
+
+    full = port(os.cpu_count() or 1)
+    entries = [full, port(1)]
+    oracle.set_threads(os.cpu_count() or 1)
+    if not pack_dir:
+        import ref_lossless
+
+        # request 0's blocks of each sampled layer (the restored, verified cache) saved the
+        # reference's way; the restore scatters them over a pool of the request's size in
+        # a seeded block order (the scatter pattern, without a 120 GB host pool for C3)
+        nb = len(ids)
+        ids_list = [int(i) for i in np.random.default_rng(5).permutation(nb)]
+        host_cache = torch.zeros((2, nb, wl.bs, wl.heads, wl.cfg.head_dim), dtype=wl.cfg.dtype)
+        saved = [ref_lossless.save_gathered(torch.index_select(wl.caches[layer], 1, wl.block_ids[0]).cpu())
+                 for layer in range(layers)]
+        done = 0
+        t0 = time.perf_counter()
+        while done < layers:
+            ref_lossless.restore_layer(saved[done], host_cache, ids_list)
+            done += 1
+            if time.perf_counter() - t0 > args.cpu_seconds:
+                break
+        dt = time.perf_counter() - t0
+        entries.append({"value": round(done * fmt.kv_bytes / dt / GB, 3), "unit": "GB/s", "cores": 1,
+                        "kind": "reference-restated",
+                        "sample": f"{done} {args.config} layers x 1 request ({done * fmt.kv_bytes / 2**20:.0f} MiB KV), "
+                                  "the reference's CPU lossless restore of the raw-bytes layout: zlib level-1 1 MiB "
+                                  f"chunks -> torch.cat -> view -> index_copy_ (one Python thread), {dt:.1f} s"})
+    return full, entries
 
 
 def run_reference(args, rank, world):
