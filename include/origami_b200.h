@@ -371,6 +371,17 @@ int32_t origami_inflate_chunks(const uint8_t* src, const int64_t* src_offsets, c
                                const int64_t* dst_lengths, int32_t threads);
 
 #ifdef __cplusplus
+/* ---------------------------------------------------------------------------------
+ * Self-test
+ * ------------------------------------------------------------------------------- */
+
+/* Runs the bounded-wait bail-out that every TMA / bulk-copy layer kernel takes when a copy
+ * does not land in time, on a wait that cannot complete (an mbarrier expecting 16 bytes that
+ * no copy delivers, nothing in flight): the kernel gives up after `polls` (1..2^22) polls,
+ * sets bit 31 of *d_error_count and returns, leaving the context usable. No counterpart in
+ * the reference, whose kernels have no waits. */
+int32_t origami_selftest_wait_timeout(uint32_t* d_error_count, int32_t polls, origami_stream_t stream);
+
 } /* extern "C" */
 #endif
 

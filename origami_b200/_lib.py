@@ -117,6 +117,8 @@ def _declare(L: ctypes.CDLL) -> None:
         _vp, i64, i64, i64, i64, i64, i64, i64, i64, i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, i32, _vp, i32, i64, i64,
         i64, P(PagedKV), i32, _vp, i64, i64, i64, i64, ctypes.c_double, _vp, _vp, _vp]
     L.origami_fused_prefix_attention_noalloc.restype = i32
+    L.origami_selftest_wait_timeout.argtypes = [_vp, i32, _vp]
+    L.origami_selftest_wait_timeout.restype = i32
     L.origami_origqz1_parse.argtypes = [_vp, i64, _vp, i64, _vp, _vp, _vp, _vp]
     L.origami_origqz1_parse.restype = i32
     L.origami_deflate_bound.argtypes = [i64]
@@ -173,6 +175,7 @@ EXPORTS = (
     "origami_deflate_bound",
     "origami_deflate_chunks",
     "origami_inflate_chunks",
+    "origami_selftest_wait_timeout",
 )
 
 ORIGAMI_DTYPE_F16 = 1

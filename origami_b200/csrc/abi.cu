@@ -861,6 +861,27 @@ int slab_grid(int64_t slabs) {
 
 }  // namespace
 
+namespace origami {
+
+// Self-test of the bounded-wait bail-out the layer kernels share (stage_wait_or_bail):
+// the mbarrier expects 16 bytes that no copy will deliver, so the CTA's wait runs out with
+// nothing in flight, and the CTA flags kWaitTimeoutFlag and leaves exactly as a layer
+// kernel whose copy never landed would.
+__global__ void selftest_wait_timeout(uint32_t* err, uint32_t polls) {
+  __shared__ __align__(8) uint64_t bar[2];
+  if (threadIdx.x == 0) {
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_expect_tx(&bar[0], 16);  // a transaction no copy completes
+  if (stage_wait_or_bail(&bar[0], 0, &bar[1], 0, false, err, polls)) return;
+  if (threadIdx.x == 0) atomicAdd(err, 1u);  // reached only if the phase completed
+}
+
+}  // namespace origami
+
 extern "C" {
 
 int32_t origami_b200_version(void) { return kVersion; }
@@ -984,6 +1005,15 @@ int32_t origami_scatter_blocks(const void* d_in, int64_t in_bytes, const origami
       static_cast<const uint8_t*>(d_in), slab, per_id, cache->num_blocks, d_block_ids, num_block_ids,
       static_cast<uint8_t*>(cache->d_data), d_error_count);
   return after_launch("scatter_slabs launch");
+}
+
+int32_t origami_selftest_wait_timeout(uint32_t* d_error_count, int32_t polls, origami_stream_t stream) {
+  if (d_error_count == nullptr) return fail(ORIGAMI_ERR_INVALID, "error word is null");
+  if (polls <= 0 || polls > static_cast<int32_t>(origami::kWaitPolls))
+    return fail(ORIGAMI_ERR_INVALID, "polls must be 1..%u", origami::kWaitPolls);
+  origami::selftest_wait_timeout<<<1, kThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      d_error_count, static_cast<uint32_t>(polls));
+  return after_launch("selftest_wait_timeout launch");
 }
 
 }  // extern "C"

@@ -177,13 +177,9 @@ __global__ void __launch_bounds__(kThreads, 2) restore_bulk(const __grid_constan
     const int s = j & 1;
     const int next = tile + 1;
     if (next < last) issue(s ^ 1, next);
-    const bool ok = mbar_wait_bounded(&bars[s], (phases >> s) & 1u);
-    if (__syncthreads_or(!ok)) {
-      if (tid == 0 && args.err) atomicOr(args.err, kWaitTimeoutFlag);
-      mbar_wait_bounded(&bars[s], (phases >> s) & 1u);
-      if (next < last) mbar_wait_bounded(&bars[s ^ 1], (phases >> (s ^ 1)) & 1u);
+    if (stage_wait_or_bail(&bars[s], (phases >> s) & 1u, &bars[s ^ 1], (phases >> (s ^ 1)) & 1u, next < last,
+                           args.err))
       return;
-    }
     phases ^= 1u << s;
     const TmaTile t = bulk_tile<BG::TT>(args, tile);
     uint8_t* rows = static_cast<uint8_t*>(args.rows[t.job]);

@@ -59,10 +59,14 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
                : "memory");
 }
 
+// Polls of a bounded mbarrier wait: far beyond any copy's latency, short enough that a
+// wait that cannot complete returns an error status in well under a minute.
+constexpr uint32_t kWaitPolls = 1u << 22;
+
 // Bounded wait for phase `parity` of an mbarrier; false when the bound ran out.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint32_t polls = kWaitPolls) {
   const uint32_t addr = smem_u32(bar);
-  for (uint32_t i = 0; i < (1u << 22); ++i) {
+  for (uint32_t i = 0; i < polls; ++i) {
     uint32_t done;
     asm volatile(
         "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
@@ -72,6 +76,24 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
     if (done) return true;
   }
   return false;
+}
+
+// Wait for a stage's copies, agreed by the whole CTA (every thread must call it). When any
+// thread's bounded wait runs out, the CTA sets kWaitTimeoutFlag in *err, waits once more
+// (bounded) for the copies it still has in flight on this stage and, when other_live, on
+// the other stage, and the caller returns: true means "leave the kernel". A copy that has
+// not landed after that second bound means the memory system itself is stuck; the CTA
+// still leaves (the flag already marks the launch's output as void) rather than wait for
+// ever. A CTA never waits on another CTA or kernel here, only on its own copies.
+__device__ __forceinline__ bool stage_wait_or_bail(uint64_t* bar, uint32_t parity, uint64_t* other,
+                                                   uint32_t other_parity, bool other_live, uint32_t* err,
+                                                   uint32_t polls = kWaitPolls) {
+  const bool ok = mbar_wait_bounded(bar, parity, polls);
+  if (!__syncthreads_or(!ok)) return false;
+  if (threadIdx.x == 0 && err) atomicOr(err, kWaitTimeoutFlag);
+  mbar_wait_bounded(bar, parity, polls);
+  if (other_live) mbar_wait_bounded(other, other_parity, polls);
+  return true;
 }
 
 __device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory"); }

@@ -269,15 +269,8 @@ __global__ void __launch_bounds__(kThreads, RAGGED ? 3 : 2) restore_rows(const _
       tn = row_tile<RG::TT>(args, cur);
       issue(s ^ 1, tn);
     }
-    const bool ok = mbar_wait_bounded(&bars[s], (phases >> s) & 1u);
-    if (__syncthreads_or(!ok)) {
-      // A copy did not land in time: flag it, wait (bounded) for this CTA's copies still
-      // in flight so that they do not outlive it, and leave. The launch's output is void.
-      if (tid == 0 && args.err) atomicOr(args.err, kWaitTimeoutFlag);
-      mbar_wait_bounded(&bars[s], (phases >> s) & 1u);
-      if (has_next) mbar_wait_bounded(&bars[s ^ 1], (phases >> (s ^ 1)) & 1u);
+    if (stage_wait_or_bail(&bars[s], (phases >> s) & 1u, &bars[s ^ 1], (phases >> (s ^ 1)) & 1u, has_next, args.err))
       return;
-    }
     phases ^= 1u << s;
 
     // Planes -> 8 token rows x 8 channels in registers.

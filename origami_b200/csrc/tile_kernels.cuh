@@ -275,14 +275,7 @@ __global__ void __launch_bounds__(kThreads) restore_tiles(const TileArgs args) {
       }
     }
   }
-  {
-    const bool ok = mbar_wait_bounded(&bar, 0);
-    if (__syncthreads_or(!ok)) {
-      if (tid == 0 && args.err) atomicOr(args.err, kWaitTimeoutFlag);
-      mbar_wait_bounded(&bar, 0);
-      return;
-    }
-  }
+  if (stage_wait_or_bail(&bar, 0, nullptr, 0, false, args.err)) return;
 
   // Phase B: 8 tokens x 8 channels per thread.
   const int A = g.A;

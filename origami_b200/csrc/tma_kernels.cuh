@@ -287,13 +287,9 @@ __global__ void __launch_bounds__(kThreads) restore_tma(const __grid_constant__ 
     const int s = j & 1;
     const int next = tile + gridDim.x;
     if (next < args.num_tiles) issue(s ^ 1, next);
-    const bool ok = mbar_wait_bounded(&bars[s], (phases >> s) & 1u);
-    if (__syncthreads_or(!ok)) {
-      if (tid == 0 && args.err) atomicOr(args.err, kWaitTimeoutFlag);
-      mbar_wait_bounded(&bars[s], (phases >> s) & 1u);
-      if (next < args.num_tiles) mbar_wait_bounded(&bars[s ^ 1], (phases >> (s ^ 1)) & 1u);
+    if (stage_wait_or_bail(&bars[s], (phases >> s) & 1u, &bars[s ^ 1], (phases >> (s ^ 1)) & 1u,
+                           next < args.num_tiles, args.err))
       return;
-    }
     phases ^= 1u << s;
     const TmaTile t = tma_tile<G::TT>(args, tile);
     uint8_t* rows = static_cast<uint8_t*>(args.rows[t.job]);
