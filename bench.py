@@ -921,6 +921,10 @@ def run_pipeline_c4(args, device, world):
     exposed = (t_pipe - t_compute) / L
     unpipe_per_layer = t_unpipe / L
     h2d_bytes = L * R * fmt.packed_bytes
+    # Lower bound of the pipelined time: layer L's GEMM needs layer L restored, so at best
+    # the restores run back to back and only the last layer's GEMM follows them (or the
+    # GEMMs run back to back behind the first restore, when compute is the longer chain).
+    t_best = max(t_restore + t_compute / L, t_compute + t_restore / L)
     return {
         "workload": f"C4 one rank at TP=8: {L} of 80 layers, 1 KV head, {R} x {T} tokens, fp16, block {bs}, "
                     "byte planes; per layer a bf16 8192x8192x8192 GEMM on the model stream",
@@ -932,6 +936,11 @@ def run_pipeline_c4(args, device, world):
         "pipelined_ms_per_layer": round(t_pipe / L, 4),
         "pcie_h2d_gbs": round(h2d_bytes / (t_restore / 1e3) / GB, 2),
         "overlap_frac_of_ideal": round((t_compute + t_restore - t_pipe) / min(t_compute, t_restore), 4),
+        # the overlap the layer dependency allows, and the share of it achieved
+        "overlap_frac_of_achievable": round((t_compute + t_restore - t_pipe) / (t_compute + t_restore - t_best), 4),
+        # floor of exposed_frac_of_unpipelined set by PCIe: a layer's H2D cannot hide behind
+        # less compute than it takes ((t_restore - t_compute) / t_unpipelined per layer)
+        "exposed_floor_frac": round(max(0.0, t_restore - t_compute) / t_unpipe, 4),
         "bytes_per_layer": R * fmt.packed_bytes,
         "ok": ok,
     }

@@ -109,6 +109,18 @@ bool sym_path(int64_t codec, int64_t group_size, int64_t kv_heads, int64_t rows)
 }
 
 // Workspace for whichever kernel a call with these shapes takes: the larger plan.
+// The shape checks of the workspace query (the launch repeats them with its own messages).
+int32_t check_plan_args(int64_t query_tokens, int64_t query_heads, int64_t kv_heads, int64_t query_start_position,
+                        int64_t sequence_length) {
+  if (query_tokens <= 0 || query_heads <= 0)
+    return fail(ORIGAMI_ERR_INVALID, "query token and head counts must be positive");
+  if (kv_heads <= 0 || query_heads % kv_heads != 0)
+    return fail(ORIGAMI_ERR_INVALID, "query_heads must be divisible by kv_heads");
+  if (sequence_length <= 0 || query_start_position < 0 || query_start_position + query_tokens > sequence_length)
+    return fail(ORIGAMI_ERR_INVALID, "query range exceeds sequence length");
+  return ORIGAMI_OK;
+}
+
 int32_t workspace_plan(int64_t query_tokens, int64_t query_heads, int64_t kv_heads, int64_t query_start,
                        int64_t sequence_length, int64_t& bytes, int64_t& counters) {
   AttnPlan p;
@@ -170,12 +182,8 @@ int32_t origami_fused_prefix_attention_workspace(int64_t query_tokens, int64_t q
                                                  int64_t query_start_position, int64_t sequence_length,
                                                  int64_t* workspace_bytes) {
   if (workspace_bytes == nullptr) return fail(ORIGAMI_ERR_INVALID, "workspace_bytes is null");
-  if (query_tokens <= 0 || query_heads <= 0)
-    return fail(ORIGAMI_ERR_INVALID, "query token and head counts must be positive");
-  if (kv_heads <= 0 || query_heads % kv_heads != 0)
-    return fail(ORIGAMI_ERR_INVALID, "query_heads must be divisible by kv_heads");
-  if (sequence_length <= 0 || query_start_position < 0 || query_start_position + query_tokens > sequence_length)
-    return fail(ORIGAMI_ERR_INVALID, "query range exceeds sequence length");
+  int32_t rc0 = check_plan_args(query_tokens, query_heads, kv_heads, query_start_position, sequence_length);
+  if (rc0) return rc0;
   int64_t bytes = 0, counters = 0;
   const int32_t rc = workspace_plan(query_tokens, query_heads, kv_heads, query_start_position, sequence_length,
                                     bytes, counters);
@@ -374,10 +382,12 @@ extern "C" int32_t origami_fused_prefix_attention_noalloc(
     int64_t prefix_tokens, int64_t query_start_position, int64_t sequence_length, double softmax_scale,
     void* d_output, uint32_t* d_error_flags, origami_stream_t stream) {
   if (cache == nullptr) return fail(ORIGAMI_ERR_INVALID, "kv cache is null");
-  int64_t need = 0;
-  int32_t rc = origami_fused_prefix_attention_workspace(query_tokens, query_heads, cache->num_heads,
-                                                        query_start_position, sequence_length, &need);
+  int32_t rc = check_plan_args(query_tokens, query_heads, cache->num_heads, query_start_position, sequence_length);
   if (rc) return rc;
+  int64_t need = 0, counters = 0;  // one plan gives both the workspace and its counters
+  if ((rc = workspace_plan(query_tokens, query_heads, cache->num_heads, query_start_position, sequence_length, need,
+                           counters)))
+    return rc;
   if (need > kStaticScratchBytes)
     return fail(ORIGAMI_ERR_UNSUPPORTED,
                 "these shapes need %lld bytes of split workspace; the static scratch holds %lld "
@@ -387,10 +397,6 @@ extern "C" int32_t origami_fused_prefix_attention_noalloc(
   if ((rc = static_scratch(&scratch))) return rc;
   if (need > 0) {
     // the arrival counters lead the workspace and must read zero at launch
-    int64_t bytes = 0, counters = 0;
-    if ((rc = workspace_plan(query_tokens, query_heads, cache->num_heads, query_start_position, sequence_length,
-                             bytes, counters)))
-      return rc;
     const cudaError_t e =
         cudaMemsetAsync(scratch, 0, static_cast<size_t>(counters), reinterpret_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(scratch counters)");

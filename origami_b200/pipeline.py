@@ -40,7 +40,10 @@ class _Slot:
 
 
 class RestorePipeline:
-    def __init__(self, device: torch.device, slot_bytes: int, slots: int = 3, *, priority: int = 0):
+    """Streams are created at high priority by default: a restore gates the model's next
+    layer, so its copy and kernel go ahead of work of normal priority when both wait."""
+
+    def __init__(self, device: torch.device, slot_bytes: int, slots: int = 3, *, priority: int = -1):
         self.device = torch.device(device)
         self.copy_stream = torch.cuda.Stream(self.device, priority=priority)
         self.restore_stream = torch.cuda.Stream(self.device, priority=priority)

@@ -95,6 +95,12 @@ def test_noalloc_rejects_plans_larger_than_the_static_array(cuda):
     c = attention_case("big_plan", 77, codec=1, bits=4, prefix=8192, kv_heads=8, query_heads=32, query_tokens=16,
                        query_start=8300)
     t = _inputs(c, cuda)
+    from origami_b200 import attention
+
+    need = attention.workspace_bytes(int(t["query"].shape[0]), int(t["query"].shape[1]), int(t["kv_cache"].shape[3]),
+                                     c["query_start"], c["sequence_length"], cuda)
+    if need <= 8 << 20:  # the split count follows the SM count; this part splits the range less
+        pytest.skip(f"this GPU's plan for the shape needs only {need} bytes")
     flags = torch.zeros(1, dtype=torch.int32, device=cuda)
     rc, _ = _noalloc(c, t, flags)
     assert rc != 0
