@@ -109,10 +109,10 @@ int32_t launch_cg_unpack(const origami::CgUnpackArgs& a, int64_t streams, cudaSt
 }
 
 // ---------------------------------------------------------------------------------------
-template <typename META, typename OUT, int D, bool UNI>
+template <typename META, typename OUT, int D, bool UNI, int BITS = 0>
 int32_t launch_kivi_tiles(origami::KiviArgs a, cudaStream_t st) {
-  using G = origami::KiviGeo<D, META>;
-  void (*fn)(origami::KiviArgs) = origami::kivi_to_cache<META, OUT, D, UNI>;
+  using G = origami::KiviGeo<D, META, BITS>;
+  void (*fn)(origami::KiviArgs) = origami::kivi_to_cache<META, OUT, D, UNI, BITS>;
   a.tiles_per_head = static_cast<int32_t>((a.tokens + G::TT - 1) / G::TT);
   const int64_t tiles = 2LL * a.H * a.tiles_per_head;
   if (tiles > 0x7FFFFFFF) return fail(ORIGAMI_ERR_UNSUPPORTED, "too many tiles");
@@ -127,6 +127,14 @@ template <typename META, typename OUT>
 int32_t launch_kivi(const origami::KiviArgs& a, bool tiled, cudaStream_t st) {
   if (tiled) {
     const bool uni = a.group_size % 8 == 0;
+    if (uni && a.bits == 2) {  // 2-bit symbols (the KIVI default): table lookups without a transpose
+      switch (a.D) {
+        case 64: return launch_kivi_tiles<META, OUT, 64, true, 2>(a, st);
+        case 128: return launch_kivi_tiles<META, OUT, 128, true, 2>(a, st);
+        case 256: return launch_kivi_tiles<META, OUT, 256, true, 2>(a, st);
+        default: break;
+      }
+    }
     switch (a.D) {
       case 64:
         return uni ? launch_kivi_tiles<META, OUT, 64, true>(a, st) : launch_kivi_tiles<META, OUT, 64, false>(a, st);

@@ -404,12 +404,15 @@ struct alignas(16) VecOf {
 // eight rows, so the two channel octets of a warp read different banks.
 constexpr int kMetaSlots = 4;
 
-template <int D, typename META>
+template <int D, typename META, int BITS = 0>
 struct KiviGeo {
   static constexpr int O = D / 8;
   static constexpr int A = kThreads / O;
   static constexpr int TT = 8 * A;
-  static constexpr int rs = TT + 24;
+  // 2-bit symbols: a run of TT symbols is TT / 4 bytes, staged as 16-byte chunks from the
+  // chunk holding its first byte (TT / 4 + 16 bytes, plus one chunk of window slack)
+  static constexpr int chunks2 = (TT / 4 + 16) / 16 + 1;
+  static constexpr int rs = BITS == 2 ? 16 * chunks2 : TT + 24;
   static constexpr int runs_bytes = D * rs;
   static constexpr int rows_off = runs_bytes + D * 4 + TT * 8;
   static constexpr int rows_bytes = TT * D * 2;
@@ -418,9 +421,9 @@ struct KiviGeo {
   static constexpr int smem_bytes = meta_off + 2 * meta_elems * static_cast<int>(sizeof(META));
 };
 
-template <typename META, typename OUT, int D, bool UNI>
+template <typename META, typename OUT, int D, bool UNI, int BITS = 0>
 __global__ void __launch_bounds__(kThreads) kivi_to_cache(const __grid_constant__ KiviArgs a) {
-  using G = KiviGeo<D, META>;
+  using G = KiviGeo<D, META, BITS>;
   extern __shared__ __align__(16) uint8_t kivi_smem[];
   uint8_t* runs = kivi_smem;
   int32_t* bit0 = reinterpret_cast<int32_t*>(kivi_smem + G::runs_bytes);
@@ -459,9 +462,31 @@ __global__ void __launch_bounds__(kThreads) kivi_to_cache(const __grid_constant_
       }
       rowoff[r] = off;
     }
-    // stage the body run of every channel: 4-byte words from the aligned word holding its
-    // first byte; bytes at or past the stream end read as zero
-    if (nbody > 0) {
+    // stage the body run of every channel; bytes at or past the stream end read as zero
+    if (BITS == 2 && nbody > 0) {
+      // 16-byte chunks from the chunk holding the run's first byte (cp.async, zero fill)
+      // (a chunk is aligned in absolute address: one that starts before the stream lies in
+      // the same 16-byte line as its first byte, and the bytes before it are never used)
+      const uintptr_t sbase = reinterpret_cast<uintptr_t>(a.stream[kv]);
+      const uintptr_t end = sbase + static_cast<uintptr_t>(a.stream_bytes[kv]);
+      const int64_t dstep = static_cast<int64_t>(kv ? 1 : a.H) * a.body_tokens * 2;  // bits between dims' runs
+      const int64_t bit_d0 = kivi_index(a, kv, h, 0, tb0 - a.sink_tokens) * 2;
+      for (int i = tid; i < D * G::chunks2; i += kThreads) {
+        const int d = i / G::chunks2;
+        const int c = i - d * G::chunks2;
+        const int64_t bitpos = bit_d0 + d * dstep;
+        const uintptr_t first = sbase + static_cast<uintptr_t>(bitpos >> 3);
+        const uintptr_t chunk = (first & ~static_cast<uintptr_t>(15)) + 16u * static_cast<uintptr_t>(c);
+        const uint32_t nbytes = chunk + 16 <= end ? 16u : (chunk < end ? static_cast<uint32_t>(end - chunk) : 0u);
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_u32(runs + d * G::rs + 16 * c)),
+                     "l"(nbytes ? chunk : (first & ~static_cast<uintptr_t>(15))), "r"(nbytes)
+                     : "memory");
+        if (c == 0) bit0[d] = static_cast<int32_t>((first & 15u) * 8u + static_cast<uintptr_t>(bitpos & 7));
+      }
+      asm volatile("cp.async.commit_group;\n" ::: "memory");
+      asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+    } else if (nbody > 0) {
+      // 4-byte words from the aligned word holding the run's first byte
       const uint8_t* s = a.stream[kv];
       const uintptr_t end = reinterpret_cast<uintptr_t>(s) + static_cast<uintptr_t>(a.stream_bytes[kv]);
       const int words = ((nbody * bits + 7) >> 3) / 4 + 2;
@@ -547,6 +572,54 @@ __global__ void __launch_bounds__(kThreads) kivi_to_cache(const __grid_constant_
             const int64_t ch = static_cast<int64_t>(h) * D + 8 * o + 2 * j;
             outw[i][j] = out_bits<OUT>(kivi_sink<META>(a, kv, t, ch)) |
                          (out_bits<OUT>(kivi_sink<META>(a, kv, t, ch + 1)) << 16);
+          }
+        }
+      } else if (BITS == 2 && UNI && staged) {
+        // 2-bit symbols, no transpose: w[c] holds channel 8o + 2c (low half) and 8o + 2c + 1
+        // (high half), 8 tokens x 2 bits each; the output word of token i and channel pair
+        // c takes the two symbols at bits 2i and 16 + 2i through a 4-entry table.
+        const int k0 = static_cast<int>(tq - tb0);
+        uint32_t w[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t half[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int d = 8 * o + 2 * c + e;
+            const int pos = bit0[d] + 2 * k0;
+            const uint32_t* row = reinterpret_cast<const uint32_t*>(runs + d * G::rs);
+            half[e] = __funnelshift_r(row[pos >> 5], row[(pos >> 5) + 1], pos & 31) & 0xFFFFu;
+          }
+          w[c] = half[0] | (half[1] << 16);
+        }
+        if (kv) {
+          // values: one (scale, zero) per token row and channel group
+          const int g = (h * D + 8 * o) / static_cast<int>(a.group_size);
+          const int base = (g - mbase) * G::TT + k0;
+          const VecOf<META> vs = *reinterpret_cast<const VecOf<META>*>(msc + base);
+          const VecOf<META> vz = *reinterpret_cast<const VecOf<META>*>(mze + base);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const uint2 t = lut4<OUT>(to_f32(vs.v[i]), to_f32(vz.v[i]));
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              const uint32_t m = (w[c] >> (2 * i)) & 0x00030003u;
+              outw[i][c] = __byte_perm(t.x, t.y, 0x1010u + 0x22u * __byte_perm(m, 0u, 0x4420u));
+            }
+          }
+        } else {
+          // keys: one (scale, zero) per channel and token group
+          const int base = (static_cast<int>(tq - a.sink_tokens) / static_cast<int>(a.group_size) - mbase) * D + 8 * o;
+          uint2 t[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) t[j] = lut4<OUT>(to_f32(msc[base + j]), to_f32(mze[base + j]));
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              const uint32_t m = (w[c] >> (2 * i)) & 0x00030003u;
+              outw[i][c] = __byte_perm(lut4_one(t[2 * c], m & 3u), lut4_one(t[2 * c + 1], m >> 16), 0x5410u);
+            }
           }
         }
       } else {

@@ -80,6 +80,13 @@ LARGE = [
     kivi_case("kivi_c2_layer_b2", 403, 32768, 128, 8, 128, 16, 2, 64, np.float16, True, False, spare_blocks=40),
     kivi_case("kivi_b4_d64_ragged", 404, 9999, 32, 4, 64, 32, 4, 32, np.float16, False, True),
     kivi_case("kivi_b3_d256", 405, 5000, 0, 2, 256, 16, 3, 128, np.float32, True, False),
+    # 2-bit symbols take the table kernel without a transpose: every head_dim, both cache
+    # layouts, fp32 metadata, truncated streams (zero-filled staging chunks), bad block ids
+    kivi_case("kivi_b2_d256_blocks_first_trunc", 406, 3001, 24, 2, 256, 16, 2, 32, np.float16, False, True,
+              trunc=(37, 5)),
+    kivi_case("kivi_b2_d64_f32_bad_ids", 407, 7777, 8, 4, 64, 32, 2, 16, np.float32, True, False, bad=True),
+    kivi_case("kivi_b2_d128_group8_no_sink", 408, 4100, 0, 3, 128, 16, 2, 8, np.float16, False, False,
+              trunc=(0, 19)),
 ]
 
 
