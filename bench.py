@@ -1314,7 +1314,7 @@ def run_quant(args, rank, world, local, impl: str):
     alg = wl.kv_bytes + wl.in_bytes
     peak, peak_kind = measured_hbm_peak()
     mean_launch = sum(launch_ms) / len(launch_ms)
-    kernel = {"CG": "cachegen_to_cache", "KIVI": "kivi_to_cache"}[kind]
+    kernel = {"CG": "cachegen_to_cache", "KIVI": "kivi2_to_cache"}[kind]  # KIVI config: 2 bits, group 64
     if impl == "reference":
         kernel = {"CG": "cachegen_unpack_dequantize_to_kv_cache_kernel",
                   "KIVI": "kivi_dequantize_to_kv_cache_kernel"}[kind]

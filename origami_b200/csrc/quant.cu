@@ -109,10 +109,18 @@ int32_t launch_cg_unpack(const origami::CgUnpackArgs& a, int64_t streams, cudaSt
 }
 
 // ---------------------------------------------------------------------------------------
-template <typename META, typename OUT, int D, bool UNI, int BITS = 0>
+// log2(v) when v is a power of two, else -1.
+int32_t ilog2_exact(int64_t v) {
+  if (v <= 0 || (v & (v - 1)) != 0) return -1;
+  int32_t s = 0;
+  while ((int64_t{1} << s) < v) ++s;
+  return s;
+}
+
+template <typename META, typename OUT, int D, bool UNI>
 int32_t launch_kivi_tiles(origami::KiviArgs a, cudaStream_t st) {
-  using G = origami::KiviGeo<D, META, BITS>;
-  void (*fn)(origami::KiviArgs) = origami::kivi_to_cache<META, OUT, D, UNI, BITS>;
+  using G = origami::KiviGeo<D, META>;
+  void (*fn)(origami::KiviArgs) = origami::kivi_to_cache<META, OUT, D, UNI>;
   a.tiles_per_head = static_cast<int32_t>((a.tokens + G::TT - 1) / G::TT);
   const int64_t tiles = 2LL * a.H * a.tiles_per_head;
   if (tiles > 0x7FFFFFFF) return fail(ORIGAMI_ERR_UNSUPPORTED, "too many tiles");
@@ -123,15 +131,31 @@ int32_t launch_kivi_tiles(origami::KiviArgs a, cudaStream_t st) {
   return launch_dependent(fn, grid, G::smem_bytes, st, a, "kivi_to_cache launch");
 }
 
+template <typename META, typename OUT, int D>
+int32_t launch_kivi2(origami::KiviArgs a, cudaStream_t st) {
+  using G = origami::Kivi2Geo<D, META>;
+  void (*fn)(origami::KiviArgs) = origami::kivi2_to_cache<META, OUT, D>;
+  a.tiles_per_head = static_cast<int32_t>((a.tokens + G::TT - 1) / G::TT);
+  const int64_t tiles = 2LL * a.H * a.tiles_per_head;
+  if (tiles > 0x7FFFFFFF) return fail(ORIGAMI_ERR_UNSUPPORTED, "too many tiles");
+  a.num_tiles = static_cast<int32_t>(tiles);
+  int grid = 0;
+  const int32_t rc = grid_for(reinterpret_cast<const void*>(fn), G::smem_bytes, tiles, grid);
+  if (rc) return rc;
+  return launch_dependent(fn, grid, G::smem_bytes, st, a, "kivi2_to_cache launch");
+}
+
 template <typename META, typename OUT>
 int32_t launch_kivi(const origami::KiviArgs& a, bool tiled, cudaStream_t st) {
   if (tiled) {
     const bool uni = a.group_size % 8 == 0;
-    if (uni && a.bits == 2) {  // 2-bit symbols (the KIVI default): table lookups without a transpose
+    const bool pow2_group = (a.group_size & (a.group_size - 1)) == 0;
+    if (uni && pow2_group && a.bits == 2) {
+      // 2-bit symbols (the KIVI default): table lookups without a transpose
       switch (a.D) {
-        case 64: return launch_kivi_tiles<META, OUT, 64, true, 2>(a, st);
-        case 128: return launch_kivi_tiles<META, OUT, 128, true, 2>(a, st);
-        case 256: return launch_kivi_tiles<META, OUT, 256, true, 2>(a, st);
+        case 64: return launch_kivi2<META, OUT, 64>(a, st);
+        case 128: return launch_kivi2<META, OUT, 128>(a, st);
+        case 256: return launch_kivi2<META, OUT, 256>(a, st);
         default: break;
       }
     }
@@ -350,6 +374,8 @@ int32_t origami_kivi_dequantize_to_kv_cache(
   a.H = static_cast<int32_t>(cache->num_heads);
   a.D = static_cast<int32_t>(cache->head_dim);
   a.err = d_error_count;
+  a.group_shift = ilog2_exact(group_size);
+  a.block_shift = ilog2_exact(cache->block_size);
   const bool tiled = sink_tokens % 8 == 0 && aligned(cache->d_data, 16);
   const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const bool bf16 = cache_dtype == ORIGAMI_DTYPE_BF16;

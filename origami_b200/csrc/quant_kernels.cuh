@@ -59,6 +59,21 @@ __device__ __forceinline__ uint32_t out_bits<__nv_bfloat16>(float v) {
   return __bfloat16_as_ushort(__float2bfloat16_rn(v));
 }
 
+// Two elements rounded to nearest-even in one paired conversion (lo in bits 0-15): the
+// same bits as two out_bits calls.
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi);
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
+  const __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
 // One symbol with the reference's bounds rule.
 __device__ __forceinline__ uint32_t symbol_at(const uint8_t* s, int64_t nbytes, int64_t index, int bits) {
   if (bits == 8) return index < nbytes ? s[index] : 0u;
@@ -316,6 +331,7 @@ struct KiviArgs {
   int64_t num_blocks, block_size, tokens, num_ids;
   int64_t sink_tokens, body_tokens, group_size, value_groups;
   int32_t bits, H, D;
+  int32_t group_shift, block_shift;  // log2 of group_size / block_size; -1: not a power of two
   int32_t tiles_per_head, num_tiles;
   uint32_t* err;
 };
@@ -383,8 +399,8 @@ __global__ void __launch_bounds__(kThreads) kivi_to_cache_elem(const __grid_cons
 // byte permute instead of an int -> float and a float -> 16-bit conversion each.
 template <typename OUT>
 __device__ __forceinline__ uint2 lut4(float scale, float zero) {
-  return make_uint2(out_bits<OUT>(__fmaf_rn(0.f, scale, zero)) | (out_bits<OUT>(__fmaf_rn(1.f, scale, zero)) << 16),
-                    out_bits<OUT>(__fmaf_rn(2.f, scale, zero)) | (out_bits<OUT>(__fmaf_rn(3.f, scale, zero)) << 16));
+  return make_uint2(pack2<OUT>(__fmaf_rn(0.f, scale, zero), __fmaf_rn(1.f, scale, zero)),
+                    pack2<OUT>(__fmaf_rn(2.f, scale, zero), __fmaf_rn(3.f, scale, zero)));
 }
 // Two elements from one table: `pair` holds symbol s0 in byte 0 and s1 in byte 1.
 __device__ __forceinline__ uint32_t lut4_pair(uint2 t, uint32_t pair) {
@@ -404,15 +420,12 @@ struct alignas(16) VecOf {
 // eight rows, so the two channel octets of a warp read different banks.
 constexpr int kMetaSlots = 4;
 
-template <int D, typename META, int BITS = 0>
+template <int D, typename META>
 struct KiviGeo {
   static constexpr int O = D / 8;
   static constexpr int A = kThreads / O;
   static constexpr int TT = 8 * A;
-  // 2-bit symbols: a run of TT symbols is TT / 4 bytes, staged as 16-byte chunks from the
-  // chunk holding its first byte (TT / 4 + 16 bytes, plus one chunk of window slack)
-  static constexpr int chunks2 = (TT / 4 + 16) / 16 + 1;
-  static constexpr int rs = BITS == 2 ? 16 * chunks2 : TT + 24;
+  static constexpr int rs = TT + 24;
   static constexpr int runs_bytes = D * rs;
   static constexpr int rows_off = runs_bytes + D * 4 + TT * 8;
   static constexpr int rows_bytes = TT * D * 2;
@@ -421,9 +434,9 @@ struct KiviGeo {
   static constexpr int smem_bytes = meta_off + 2 * meta_elems * static_cast<int>(sizeof(META));
 };
 
-template <typename META, typename OUT, int D, bool UNI, int BITS = 0>
+template <typename META, typename OUT, int D, bool UNI>
 __global__ void __launch_bounds__(kThreads) kivi_to_cache(const __grid_constant__ KiviArgs a) {
-  using G = KiviGeo<D, META, BITS>;
+  using G = KiviGeo<D, META>;
   extern __shared__ __align__(16) uint8_t kivi_smem[];
   uint8_t* runs = kivi_smem;
   int32_t* bit0 = reinterpret_cast<int32_t*>(kivi_smem + G::runs_bytes);
@@ -463,29 +476,7 @@ __global__ void __launch_bounds__(kThreads) kivi_to_cache(const __grid_constant_
       rowoff[r] = off;
     }
     // stage the body run of every channel; bytes at or past the stream end read as zero
-    if (BITS == 2 && nbody > 0) {
-      // 16-byte chunks from the chunk holding the run's first byte (cp.async, zero fill)
-      // (a chunk is aligned in absolute address: one that starts before the stream lies in
-      // the same 16-byte line as its first byte, and the bytes before it are never used)
-      const uintptr_t sbase = reinterpret_cast<uintptr_t>(a.stream[kv]);
-      const uintptr_t end = sbase + static_cast<uintptr_t>(a.stream_bytes[kv]);
-      const int64_t dstep = static_cast<int64_t>(kv ? 1 : a.H) * a.body_tokens * 2;  // bits between dims' runs
-      const int64_t bit_d0 = kivi_index(a, kv, h, 0, tb0 - a.sink_tokens) * 2;
-      for (int i = tid; i < D * G::chunks2; i += kThreads) {
-        const int d = i / G::chunks2;
-        const int c = i - d * G::chunks2;
-        const int64_t bitpos = bit_d0 + d * dstep;
-        const uintptr_t first = sbase + static_cast<uintptr_t>(bitpos >> 3);
-        const uintptr_t chunk = (first & ~static_cast<uintptr_t>(15)) + 16u * static_cast<uintptr_t>(c);
-        const uint32_t nbytes = chunk + 16 <= end ? 16u : (chunk < end ? static_cast<uint32_t>(end - chunk) : 0u);
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_u32(runs + d * G::rs + 16 * c)),
-                     "l"(nbytes ? chunk : (first & ~static_cast<uintptr_t>(15))), "r"(nbytes)
-                     : "memory");
-        if (c == 0) bit0[d] = static_cast<int32_t>((first & 15u) * 8u + static_cast<uintptr_t>(bitpos & 7));
-      }
-      asm volatile("cp.async.commit_group;\n" ::: "memory");
-      asm volatile("cp.async.wait_group 0;\n" ::: "memory");
-    } else if (nbody > 0) {
+    if (nbody > 0) {
       // 4-byte words from the aligned word holding the run's first byte
       const uint8_t* s = a.stream[kv];
       const uintptr_t end = reinterpret_cast<uintptr_t>(s) + static_cast<uintptr_t>(a.stream_bytes[kv]);
@@ -572,54 +563,6 @@ __global__ void __launch_bounds__(kThreads) kivi_to_cache(const __grid_constant_
             const int64_t ch = static_cast<int64_t>(h) * D + 8 * o + 2 * j;
             outw[i][j] = out_bits<OUT>(kivi_sink<META>(a, kv, t, ch)) |
                          (out_bits<OUT>(kivi_sink<META>(a, kv, t, ch + 1)) << 16);
-          }
-        }
-      } else if (BITS == 2 && UNI && staged) {
-        // 2-bit symbols, no transpose: w[c] holds channel 8o + 2c (low half) and 8o + 2c + 1
-        // (high half), 8 tokens x 2 bits each; the output word of token i and channel pair
-        // c takes the two symbols at bits 2i and 16 + 2i through a 4-entry table.
-        const int k0 = static_cast<int>(tq - tb0);
-        uint32_t w[4];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t half[2];
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int d = 8 * o + 2 * c + e;
-            const int pos = bit0[d] + 2 * k0;
-            const uint32_t* row = reinterpret_cast<const uint32_t*>(runs + d * G::rs);
-            half[e] = __funnelshift_r(row[pos >> 5], row[(pos >> 5) + 1], pos & 31) & 0xFFFFu;
-          }
-          w[c] = half[0] | (half[1] << 16);
-        }
-        if (kv) {
-          // values: one (scale, zero) per token row and channel group
-          const int g = (h * D + 8 * o) / static_cast<int>(a.group_size);
-          const int base = (g - mbase) * G::TT + k0;
-          const VecOf<META> vs = *reinterpret_cast<const VecOf<META>*>(msc + base);
-          const VecOf<META> vz = *reinterpret_cast<const VecOf<META>*>(mze + base);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const uint2 t = lut4<OUT>(to_f32(vs.v[i]), to_f32(vz.v[i]));
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-              const uint32_t m = (w[c] >> (2 * i)) & 0x00030003u;
-              outw[i][c] = __byte_perm(t.x, t.y, 0x1010u + 0x22u * __byte_perm(m, 0u, 0x4420u));
-            }
-          }
-        } else {
-          // keys: one (scale, zero) per channel and token group
-          const int base = (static_cast<int>(tq - a.sink_tokens) / static_cast<int>(a.group_size) - mbase) * D + 8 * o;
-          uint2 t[8];
-#pragma unroll
-          for (int j = 0; j < 8; ++j) t[j] = lut4<OUT>(to_f32(msc[base + j]), to_f32(mze[base + j]));
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-              const uint32_t m = (w[c] >> (2 * i)) & 0x00030003u;
-              outw[i][c] = __byte_perm(lut4_one(t[2 * c], m & 3u), lut4_one(t[2 * c + 1], m >> 16), 0x5410u);
-            }
           }
         }
       } else {
@@ -759,4 +702,285 @@ __global__ void __launch_bounds__(kThreads) kivi_to_cache(const __grid_constant_
   }
 }
 
+
+// ---------------------------------------------------------------------------------------
+// 2-bit KIVI (the reference's default width) -> paged cache
+//
+// Same tiles and thread mapping as kivi_to_cache (CTA = (kv, head, TT tokens) x D
+// channels, a thread = 8 tokens x 8 channels), without a transpose: a thread's channel
+// runs are read as 16-bit fields (8 tokens x 2 bits), two channels are interleaved into one
+// word by a byte permute, and each output word (two channels of one token) is a byte
+// permute of a 4-entry table fma(s, scale, zero), s = 0..3, whose selector is built for two
+// tokens at once by one multiply-add. Runs are staged by 16-byte cp.async chunks; finished
+// token rows leave shared memory as whole-row bulk copies (one per row, issued by the
+// thread that owns the row), drained only before the next tile's rows are written.
+//
+// Tiles run head-fastest (tile = h + H * (tt + tiles_per_head * kv)): the CTAs in flight
+// write all heads of the same token rows (whole cache rows, DRAM-page friendly) and read
+// consecutive stretches of every channel run. Group and block sizes are powers of two
+// (shifts); token counts are below 2^31.
+// ---------------------------------------------------------------------------------------
+template <int D, typename META>
+struct Kivi2Geo {
+  static constexpr int O = D / 8;
+  static constexpr int A = kThreads / O;
+  static constexpr int TT = 8 * A;  // at most kThreads: thread r owns token row r
+  // a run of TT symbols is TT / 4 bytes, staged from the 16-byte chunk holding its first
+  // byte, with one chunk of slack for the 64-bit window at its end
+  static constexpr int chunks = (TT / 4 + 16) / 16 + 1;
+  static constexpr int rs = 16 * chunks;
+  static constexpr int row_bytes = D * 2;
+  // token rows with 16 bytes of padding after every 8 rows: the 8 rows a thread writes
+  // land in different banks for the threads of a quarter warp, and every row stays
+  // 16-byte aligned for its bulk copy
+  static constexpr int rows_bytes = TT * row_bytes + (TT / 8) * 16;
+  static constexpr int runs_off = rows_bytes;
+  static constexpr int bit0_off = runs_off + D * rs;
+  static constexpr int meta_off = bit0_off + D * 4;
+  // (scale, zero): values as [group slot][token], keys as [group slot][channel]
+  static constexpr int meta_elems = kMetaSlots * (TT > D ? TT : D);
+  static constexpr int smem_bytes = meta_off + 2 * meta_elems * static_cast<int>(sizeof(META));
+  // 5 CTAs an SM where their shared memory fits (1 KB reserved per CTA of 228 KB), else 4
+  static constexpr int min_ctas = 5 * (smem_bytes + 1024) <= 228 * 1024 ? 5 : 4;
+  static_assert(TT <= kThreads, "one token row per thread");
+};
+
+// Permute selectors of tokens k (bits 0-15) and k + 4 (bits 16-31) from a word holding
+// channel A's and channel B's symbols as bytes [A 0-3, B 0-3, A 4-7, B 4-7]: byte j of the
+// masked word is a symbol s, and 0x22 * s + 0x10 is the selector nibble pair (2s, 2s + 1).
+__device__ __forceinline__ uint32_t kivi2_selectors(uint32_t w2, int k) {
+  return ((w2 >> (2 * k)) & 0x03030303u) * 0x22u + 0x10101010u;
+}
+
+template <typename META, typename OUT, int D>
+__global__ void __launch_bounds__(kThreads, Kivi2Geo<D, META>::min_ctas) kivi2_to_cache(const __grid_constant__ KiviArgs a) {
+  using G = Kivi2Geo<D, META>;
+  extern __shared__ __align__(128) uint8_t kivi2_smem[];
+  uint8_t* rows_sm = kivi2_smem;
+  uint8_t* runs = kivi2_smem + G::runs_off;
+  int32_t* bit0 = reinterpret_cast<int32_t*>(kivi2_smem + G::bit0_off);
+  META* msc = reinterpret_cast<META*>(kivi2_smem + G::meta_off);
+  META* mze = msc + G::meta_elems;
+  const int tid = threadIdx.x;
+  const int64_t C = static_cast<int64_t>(a.H) * D;
+  const int ao = tid % G::A;
+  const int o = tid / G::A;
+  const int gs = a.group_shift;
+  const int sink = static_cast<int>(a.sink_tokens);
+  const int tokens = static_cast<int>(a.tokens);
+  dependent_launch_entry();
+
+  // tile = h + H * r, r = tt + tiles_per_head * kv; advanced by gridDim.x without divisions
+  const int tph = a.tiles_per_head;
+  const int step_h = static_cast<int>(gridDim.x) % a.H;
+  const int step_r = static_cast<int>(gridDim.x) / a.H;
+  int h = static_cast<int>(blockIdx.x) % a.H;
+  int r = static_cast<int>(blockIdx.x) / a.H;
+  for (int tile = blockIdx.x; tile < a.num_tiles; tile += gridDim.x) {
+    const int kv = r >= tph ? 1 : 0;
+    const int t0 = (r - kv * tph) * G::TT;
+    const int tb0 = max(t0, sink);
+    const int tb1 = min(t0 + G::TT, tokens);
+    const int nbody = max(tb1 - tb0, 0);
+
+    // this thread's cache row: token t0 + tid, through the block table (-1: not written)
+    int64_t off = -1;
+    if (tid < G::TT) {
+      const int t = t0 + tid;
+      if (t < tokens) {
+        const int bi = a.block_shift >= 0 ? t >> a.block_shift : t / static_cast<int>(a.block_size);
+        const int64_t blk = a.ids[bi];
+        if (blk < 0 || blk >= a.num_blocks) {
+          if (a.err) atomicAdd(a.err, 1u);
+        } else {
+          off = kv * a.kv_stride + blk * a.block_stride +
+                static_cast<int64_t>(t - bi * static_cast<int>(a.block_size)) * a.token_stride +
+                static_cast<int64_t>(h) * a.head_stride;
+        }
+      }
+    }
+    // stage the body run of every channel as 16-byte chunks from the chunk holding its
+    // first byte (aligned in absolute address, so a chunk that starts before the stream
+    // shares a 16-byte line with the run's first byte; bytes at or past the stream end read
+    // as zero through the cp.async source size)
+    if (nbody > 0) {
+      const uintptr_t sbase = reinterpret_cast<uintptr_t>(a.stream[kv]);
+      const uintptr_t end = sbase + static_cast<uintptr_t>(a.stream_bytes[kv]);
+      const int64_t dstep = static_cast<int64_t>(kv ? 1 : a.H) * a.body_tokens * 2;  // bits between dims' runs
+      const int64_t bit_d0 = kivi_index(a, kv, h, 0, tb0 - sink) * 2;
+#pragma unroll
+      for (int i = tid; i < D * G::chunks; i += kThreads) {
+        const int d = i / G::chunks;
+        const int c = i % G::chunks;
+        const int64_t bitpos = bit_d0 + d * dstep;
+        const uintptr_t first = sbase + static_cast<uintptr_t>(bitpos >> 3);
+        const uintptr_t line = first & ~static_cast<uintptr_t>(15);
+        const uintptr_t chunk = line + 16u * static_cast<uintptr_t>(c);
+        const uint32_t nbytes = chunk + 16 <= end ? 16u : (chunk < end ? static_cast<uint32_t>(end - chunk) : 0u);
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_u32(runs + d * G::rs + 16 * c)),
+                     "l"(nbytes ? chunk : line), "r"(nbytes)
+                     : "memory");
+        if (c == 0) bit0[d] = static_cast<int32_t>((first & 15u) * 8u + static_cast<uintptr_t>(bitpos & 7));
+      }
+      asm volatile("cp.async.commit_group;\n" ::: "memory");
+    }
+    // this tile's scale / zero in shared memory when they fit in kMetaSlots value groups
+    // ([group slot][token]) or key groups ([group slot][channel]); otherwise the
+    // dequantization reads them from global memory
+    bool staged = false;
+    int mbase = 0;  // first staged value group / key group
+    if (nbody > 0) {
+      const META* sc = static_cast<const META*>(a.scale[kv]);
+      const META* ze = static_cast<const META*>(a.zero[kv]);
+      if (kv) {
+        mbase = (h * D) >> gs;
+        const int ng = ((h * D + D - 1) >> gs) - mbase + 1;
+        if (ng <= kMetaSlots) {
+          staged = true;
+          for (int e = tid; e < ng * G::TT; e += kThreads) {
+            const int g = e / G::TT;
+            const int rr = e % G::TT;
+            if (rr < nbody) {
+              const int64_t idx = static_cast<int64_t>(tb0 - sink + rr) * a.value_groups + mbase + g;
+              msc[e] = sc[idx];
+              mze[e] = ze[idx];
+            }
+          }
+        }
+      } else {
+        mbase = (tb0 - sink) >> gs;
+        const int nkg = ((tb1 - 1 - sink) >> gs) - mbase + 1;
+        if (nkg <= kMetaSlots) {
+          staged = true;
+          for (int e = tid; e < nkg * D; e += kThreads) {
+            const int64_t idx = static_cast<int64_t>(mbase + e / D) * C + h * D + (e % D);
+            msc[e] = sc[idx];
+            mze[e] = ze[idx];
+          }
+        }
+      }
+      asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+    }
+    // the previous tile's rows have been read out of shared memory by their bulk copies
+    if (tid < G::TT) asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory");
+    __syncthreads();
+
+    const int tq = t0 + 8 * ao;  // first token of this thread's octet
+    if (tq < tokens) {
+      uint32_t outw[8][4];
+      const int ch0 = h * D + 8 * o;
+      if (tq < sink) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int t = min(tq + i, tokens - 1);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            outw[i][j] = pack2<OUT>(kivi_sink<META>(a, kv, t, ch0 + 2 * j), kivi_sink<META>(a, kv, t, ch0 + 2 * j + 1));
+        }
+      } else {
+        // w2[c]: channels 8o + 2c (A) and 8o + 2c + 1 (B) as bytes [A 0-3, B 0-3, A 4-7, B 4-7]
+        // of tokens tq .. tq + 7, 2 bits each
+        const int k0 = tq - tb0;
+        uint32_t w2[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t f[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int d = 8 * o + 2 * c + e;
+            const int pos = bit0[d] + 2 * k0;
+            const uint32_t* row = reinterpret_cast<const uint32_t*>(runs + d * G::rs);
+            f[e] = __funnelshift_r(row[pos >> 5], row[(pos >> 5) + 1], pos & 31);
+          }
+          w2[c] = __byte_perm(f[0], f[1], 0x5140u);
+        }
+        const int bq = tq - sink;
+        const META* sc = static_cast<const META*>(a.scale[kv]);
+        const META* ze = static_cast<const META*>(a.zero[kv]);
+        if (kv) {
+          // values: one (scale, zero) per token and channel group, one table per token
+          const int g = ch0 >> gs;
+          VecOf<META> vs, vz;
+          if (staged) {  // tokens k0 .. k0 + 7 of group g (k0 % 8 == 0): one vector each
+            const int base = (g - mbase) * G::TT + k0;
+            vs = *reinterpret_cast<const VecOf<META>*>(msc + base);
+            vz = *reinterpret_cast<const VecOf<META>*>(mze + base);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int64_t idx = static_cast<int64_t>(min(bq + i, static_cast<int>(a.body_tokens) - 1)) *
+                                      a.value_groups + g;
+              vs.v[i] = sc[idx];
+              vz.v[i] = ze[idx];
+            }
+          }
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint2 tl = lut4<OUT>(to_f32(vs.v[k]), to_f32(vz.v[k]));
+            const uint2 th = lut4<OUT>(to_f32(vs.v[k + 4]), to_f32(vz.v[k + 4]));
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              const uint32_t y = kivi2_selectors(w2[c], k);
+              outw[k][c] = __byte_perm(tl.x, tl.y, y);
+              outw[k + 4][c] = __byte_perm(th.x, th.y, y >> 16);
+            }
+          }
+        } else {
+          // keys: one (scale, zero) per channel and token group, one table per channel;
+          // channel A's table gives the low half of a word, channel B's the high half
+          VecOf<META> vs, vz;
+          if (staged) {
+            const int base = ((bq >> gs) - mbase) * D + 8 * o;
+            vs = *reinterpret_cast<const VecOf<META>*>(msc + base);
+            vz = *reinterpret_cast<const VecOf<META>*>(mze + base);
+          } else {
+            const int64_t base = static_cast<int64_t>(bq >> gs) * C + ch0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              vs.v[j] = sc[base + j];
+              vz.v[j] = ze[base + j];
+            }
+          }
+          uint2 t[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) t[j] = lut4<OUT>(to_f32(vs.v[j]), to_f32(vz.v[j]));
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              const uint32_t y = kivi2_selectors(w2[c], k);
+              const uint32_t yh = y >> 16;
+              outw[k][c] = __byte_perm(__byte_perm(t[2 * c].x, t[2 * c].y, y),
+                                       __byte_perm(t[2 * c + 1].x, t[2 * c + 1].y, y), 0x7610u);
+              outw[k + 4][c] = __byte_perm(__byte_perm(t[2 * c].x, t[2 * c].y, yh),
+                                           __byte_perm(t[2 * c + 1].x, t[2 * c + 1].y, yh), 0x7610u);
+            }
+          }
+        }
+      }
+      uint8_t* dst = rows_sm + 8 * ao * G::row_bytes + 16 * (ao + o);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        *reinterpret_cast<uint4*>(dst + i * G::row_bytes) = make_uint4(outw[i][0], outw[i][1], outw[i][2], outw[i][3]);
+    }
+    // rows written by the generic proxy, read by the bulk copies
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+    __syncthreads();
+    if (tid < G::TT) {
+      if (off >= 0)
+        asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;\n" ::"l"(a.cache + 2 * off),
+                     "r"(smem_u32(rows_sm + tid * G::row_bytes + 16 * (tid >> 3))), "r"(G::row_bytes)
+                     : "memory");
+      asm volatile("cp.async.bulk.commit_group;\n" ::: "memory");
+    }
+    h += step_h;
+    r += step_r;
+    if (h >= a.H) {
+      h -= a.H;
+      ++r;
+    }
+  }
+  // the last rows are in global memory before the CTA leaves
+  if (tid < G::TT) asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory");
+}
 }  // namespace origami

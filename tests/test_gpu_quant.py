@@ -87,6 +87,10 @@ LARGE = [
     kivi_case("kivi_b2_d64_f32_bad_ids", 407, 7777, 8, 4, 64, 32, 2, 16, np.float32, True, False, bad=True),
     kivi_case("kivi_b2_d128_group8_no_sink", 408, 4100, 0, 3, 128, 16, 2, 8, np.float16, False, False,
               trunc=(0, 19)),
+    # block size that is not a power of two (block index by division), and a group size that
+    # is not one (the general tile kernel)
+    kivi_case("kivi_b2_bs24", 409, 2000, 16, 2, 128, 24, 2, 32, np.float16, True, False),
+    kivi_case("kivi_b2_group24", 410, 1500, 8, 2, 64, 16, 2, 24, np.float16, True, False),
 ]
 
 
