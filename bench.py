@@ -1314,7 +1314,8 @@ def run_quant(args, rank, world, local, impl: str):
     alg = wl.kv_bytes + wl.in_bytes
     peak, peak_kind = measured_hbm_peak()
     mean_launch = sum(launch_ms) / len(launch_ms)
-    kernel = {"CG": "cachegen_to_cache", "KIVI": "kivi2_to_cache"}[kind]  # KIVI config: 2 bits, group 64
+    # the configs' kernels: CG 5 / 4-bit symbols (staged rows), KIVI 2 bits with group 64
+    kernel = {"CG": "cachegen_staged", "KIVI": "kivi2_to_cache"}[kind]
     if impl == "reference":
         kernel = {"CG": "cachegen_unpack_dequantize_to_kv_cache_kernel",
                   "KIVI": "kivi_dequantize_to_kv_cache_kernel"}[kind]

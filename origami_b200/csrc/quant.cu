@@ -89,8 +89,43 @@ int32_t launch_cg(const origami::CgArgs& a, cudaStream_t st) {
   return launch_dependent(fn, grid, 0, st, a, "cachegen_to_cache launch");
 }
 
+// Staged rows (symbols of at most 5 bits, 16-byte vector rows); null when the stages
+// would not fit.
 template <typename MAXT, typename OUT>
-int32_t launch_cg_vec(bool vec, const origami::CgArgs& a, cudaStream_t st) {
+int32_t launch_cg_staged(const origami::CgArgs& a, const uint8_t* buf_end, cudaStream_t st, bool& launched) {
+  launched = false;
+  const int64_t rb = static_cast<int64_t>(a.nvec) * std::max(a.bits[0], a.bits[1]);
+  const int stage_bytes = origami::CgStageGeo::bytes_for(rb);
+  if (2LL * stage_bytes > 96 * 1024) return ORIGAMI_OK;
+  void (*fn)(origami::CgArgs, int, const uint8_t*) = origami::cachegen_staged<MAXT, OUT>;
+  const int smem = 2 * stage_bytes;
+  int grid = 0;
+  const int64_t groups = 2 * ((a.tokens + origami::kCgGroupRows - 1) / origami::kCgGroupRows);
+  const int32_t rc = grid_for(reinterpret_cast<const void*>(fn), smem, groups, grid);
+  if (rc) return rc;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  launched = true;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, fn, a, stage_bytes, buf_end);
+  if (e != cudaSuccess) return cuda_fail(e, "cachegen_staged launch");
+  return after_launch("cachegen_staged launch");
+}
+
+template <typename MAXT, typename OUT>
+int32_t launch_cg_vec(bool vec, const origami::CgArgs& a, const uint8_t* buf_end, cudaStream_t st) {
+  if (vec && a.bits[0] <= 5 && a.bits[1] <= 5) {
+    bool launched = false;
+    const int32_t rc = launch_cg_staged<MAXT, OUT>(a, buf_end, st, launched);
+    if (rc || launched) return rc;
+  }
   return vec ? launch_cg<MAXT, OUT, true>(a, st) : launch_cg<MAXT, OUT, false>(a, st);
 }
 
@@ -242,9 +277,12 @@ int32_t origami_cachegen_unpack_dequantize_to_kv_cache(
   a.err = d_error_count;
   const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const bool bf16 = cache_dtype == ORIGAMI_DTYPE_BF16;
+  const uint8_t* buf_end = d_bytestream + bytestream_bytes;
   if (max_dtype == ORIGAMI_DTYPE_F16)
-    return bf16 ? launch_cg_vec<__half, __nv_bfloat16>(vec, a, st) : launch_cg_vec<__half, __half>(vec, a, st);
-  return bf16 ? launch_cg_vec<float, __nv_bfloat16>(vec, a, st) : launch_cg_vec<float, __half>(vec, a, st);
+    return bf16 ? launch_cg_vec<__half, __nv_bfloat16>(vec, a, buf_end, st)
+                : launch_cg_vec<__half, __half>(vec, a, buf_end, st);
+  return bf16 ? launch_cg_vec<float, __nv_bfloat16>(vec, a, buf_end, st)
+              : launch_cg_vec<float, __half>(vec, a, buf_end, st);
 }
 
 int32_t origami_cachegen_unpack_dequantize(

@@ -248,6 +248,174 @@ __global__ void __launch_bounds__(kThreads) cachegen_to_cache(const __grid_const
   }
 }
 
+// Staged CacheGen -> paged cache (VEC rows, symbols of at most 5 bits on both streams).
+//
+// Rows are taken in groups of kCgGroupRows consecutive tokens of one stream. A group's
+// symbol bytes are contiguous, so one thread brings them into shared memory with one bulk
+// copy (from the 16-byte line holding the first byte; two stages, bounded mbarrier waits),
+// and the group's max values and block ids are fetched into registers one group ahead. A
+// warp decodes kCgRowsPerWarp rows from shared memory: lane l's fields of vectors l + 32 i
+// (one routine per symbol width), the shuffle lookup of cachegen_to_cache (each lane
+// computes the finished element for one symbol value), one 16-byte store per vector. A
+// group whose bytes reach the stream's read limit or the end of the bytestream is decoded
+// from global memory, with the reference's bounds rule, instead. 32-row groups and 4 CTAs
+// an SM (64 registers) measured fastest (8- and 16-row groups pay the group barriers and
+// fetches too often; 64-row stages leave 2 CTAs an SM).
+constexpr int kCgRowsPerWarp = 4;
+constexpr int kCgGroupRows = kCgRowsPerWarp * (kThreads / 32);
+
+struct CgStageGeo {
+  // per stage: kCgGroupRows rows of the wider stream + one line + 8 bytes of read slack
+  __host__ __device__ static int bytes_for(int64_t row_bytes) {
+    return static_cast<int>(((kCgGroupRows * row_bytes + 16 + 8) + 127) / 128 * 128);
+  }
+};
+
+// The 8 * BITS bits of a vector's symbols from byte p of a staged row (BITS <= 5, so they
+// lie in the two aligned 32-bit words from p & ~3; the stage has 8 bytes of read slack).
+template <int BITS>
+__device__ __forceinline__ uint64_t field_from_smem(const uint8_t* p) {
+  static_assert(BITS <= 5, "a field of at most 40 bits");
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(a & ~static_cast<uintptr_t>(3));
+  const int sh = static_cast<int>(a & 3) * 8;
+  const uint32_t w0 = w[0], w1 = w[1];
+  return (static_cast<uint64_t>(w1 >> sh) << 32) | __funnelshift_r(w0, w1, sh);
+}
+
+// One staged row of BITS-bit symbols: lane l's vectors l, l + 32, ... from shared memory.
+template <int BITS, typename OUT>
+__device__ __forceinline__ void cg_row_smem(const uint8_t* row, int nvec, uint32_t lut, OUT* dst, int lane) {
+  for (int v0 = 0; v0 < nvec; v0 += 32) {
+    const int v = v0 + lane;
+    const uint64_t field = v < nvec ? field_from_smem<BITS>(row + v * BITS) : 0;
+    const uint4 out = lookup8_shfl(lut, field, BITS);
+    if (v < nvec) st_global_cs16(dst + 8 * v, out);
+  }
+}
+
+template <typename MAXT, typename OUT>
+__global__ void __launch_bounds__(kThreads, 4) cachegen_staged(const __grid_constant__ CgArgs a, int stage_bytes,
+                                                          const uint8_t* buf_end) {
+  __shared__ float table[2][256];
+  __shared__ float gmax[2][kCgGroupRows];
+  __shared__ int64_t gblk[2][kCgGroupRows];
+  __shared__ __align__(8) uint64_t bars[2];
+  extern __shared__ __align__(128) uint8_t cg_stage[];
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int64_t gpk = (a.tokens + kCgGroupRows - 1) / kCgGroupRows;  // groups per stream
+  const int64_t groups = 2 * gpk;
+  const int64_t step = gridDim.x;
+  if (tid == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    fence_mbar_init();
+  }
+  dependent_launch_entry();
+  cg_table(table, a.bins);  // (ends with a barrier: the mbarriers are initialised for all)
+  int64_t g = blockIdx.x;
+  if (g >= groups) return;
+
+  // Issue group gg into stage s: thread 0 starts the bulk copy (or arrives without bytes
+  // when the group takes the global path); threads below kCgGroupRows fetch their row's
+  // max and block id into registers. Returns the group's byte offset into the stage (-1:
+  // global path).
+  float pm = 0.f;
+  int64_t pb = 0;
+  auto issue = [&](int64_t gg, int s) -> int {
+    const int kv = gg >= gpk ? 1 : 0;
+    const int64_t r0 = (gg - kv * gpk) * kCgGroupRows;
+    const int64_t r1 = min64(r0 + kCgGroupRows, a.tokens);
+    const int64_t rb = static_cast<int64_t>(a.nvec) * a.bits[kv];  // bytes of a row
+    const uintptr_t first = reinterpret_cast<uintptr_t>(a.stream[kv]) + static_cast<uintptr_t>(r0 * rb);
+    const uintptr_t end = reinterpret_cast<uintptr_t>(a.stream[kv]) + static_cast<uintptr_t>(r1 * rb);
+    const uintptr_t lo = first & ~static_cast<uintptr_t>(15);
+    const uintptr_t hi = (end + 15) & ~static_cast<uintptr_t>(15);
+    const bool fast = r1 * rb <= a.stream_bytes[kv] && hi <= reinterpret_cast<uintptr_t>(buf_end);
+    if (tid == 0) {
+      if (fast) {
+        mbar_expect_tx(&bars[s], static_cast<uint32_t>(hi - lo));
+        bulk_load(cg_stage + s * stage_bytes, reinterpret_cast<const void*>(lo), static_cast<uint32_t>(hi - lo),
+                  &bars[s]);
+      } else {
+        mbar_arrive(&bars[s]);
+      }
+    }
+    if (tid < kCgGroupRows) {
+      const int64_t t = r0 + tid;
+      if (t < a.tokens) {
+        pm = to_f32(static_cast<const MAXT*>(a.maxv[kv])[t]);
+        pb = a.ids[static_cast<int32_t>(t) / static_cast<int32_t>(a.block_size)];
+      }
+    }
+    return fast ? static_cast<int>(first - lo) : -1;
+  };
+
+  int off_cur = issue(g, 0);
+  if (tid < kCgGroupRows) {
+    gmax[0][tid] = pm;
+    gblk[0][tid] = pb;
+  }
+  uint32_t phases = 0;
+  for (int j = 0;; ++j, g += step) {
+    const int s = j & 1;
+    const bool has_next = g + step < groups;
+    __syncthreads();  // stage s ^ 1 and its max / block ids are free; stage s's are written
+    const int off_next = has_next ? issue(g + step, s ^ 1) : -1;
+    if (stage_wait_or_bail(&bars[s], (phases >> s) & 1u, &bars[s ^ 1], (phases >> (s ^ 1)) & 1u, has_next, a.err))
+      return;
+    phases ^= 1u << s;
+
+    const int kv = g >= gpk ? 1 : 0;
+#pragma unroll 1
+    for (int k = 0; k < kCgRowsPerWarp; ++k) {
+      const int rr = warp + k * (kThreads / 32);  // row of the group
+      const int64_t t = (g - kv * gpk) * kCgGroupRows + rr;
+      if (t >= a.tokens) break;
+      const int bits = a.bits[kv];
+      const int64_t blk = gblk[s][rr];
+      if (blk < 0 || blk >= a.num_blocks) {  // counted per (kv, token, head) row
+        if (lane == 0 && a.err) atomicAdd(a.err, static_cast<uint32_t>(a.heads));
+      } else {
+        const int64_t bi = static_cast<int32_t>(t) / static_cast<int32_t>(a.block_size);
+        OUT* dst = reinterpret_cast<OUT*>(a.cache) + kv * a.kv_stride + blk * a.block_stride +
+                   (t - bi * a.block_size) * a.token_stride;
+        const uint32_t lut = out_bits<OUT>(table[kv][lane] * gmax[s][rr]);
+        if (off_cur >= 0) {
+          const uint8_t* row = cg_stage + s * stage_bytes + off_cur + rr * a.nvec * bits;
+          switch (bits) {  // warp-uniform
+            case 5: cg_row_smem<5, OUT>(row, a.nvec, lut, dst, lane); break;
+            case 4: cg_row_smem<4, OUT>(row, a.nvec, lut, dst, lane); break;
+            case 3: cg_row_smem<3, OUT>(row, a.nvec, lut, dst, lane); break;
+            case 2: cg_row_smem<2, OUT>(row, a.nvec, lut, dst, lane); break;
+            default: cg_row_smem<1, OUT>(row, a.nvec, lut, dst, lane); break;
+          }
+        } else {
+          // the group reaches the stream's read limit: global loads with the bounds rule
+          const uint8_t* gs = a.stream[kv];
+          const int64_t nb = a.stream_bytes[kv];
+          const int64_t k0 = t * a.nvec;
+          switch (bits) {
+            case 5: cg_row_shfl<5, OUT>(gs, nb, k0, a.nvec, lut, dst, lane); break;
+            case 4: cg_row_shfl<4, OUT>(gs, nb, k0, a.nvec, lut, dst, lane); break;
+            case 3: cg_row_shfl<3, OUT>(gs, nb, k0, a.nvec, lut, dst, lane); break;
+            case 2: cg_row_shfl<2, OUT>(gs, nb, k0, a.nvec, lut, dst, lane); break;
+            default: cg_row_shfl<1, OUT>(gs, nb, k0, a.nvec, lut, dst, lane); break;
+          }
+        }
+      }
+    }
+    if (!has_next) break;
+    if (tid < kCgGroupRows) {
+      gmax[s ^ 1][tid] = pm;
+      gblk[s ^ 1][tid] = pb;
+    }
+    off_cur = off_next;
+  }
+}
+
 // ---------------------------------------------------------------------------------------
 // CacheGen -> [layers, 2, heads, tokens, head_dim] fp16 (no cache)
 // ---------------------------------------------------------------------------------------

@@ -77,6 +77,11 @@ def test_matches_oracle_and_reference(cuda, case, ref_ext):
 LARGE = [
     cachegen_cache_case("cg_c2_layer", 401, 32768, 8, 128, 16, 5, 4, 32, 16, np.float16, True, False, spare_blocks=40),
     cachegen_cache_case("cg_c2_layer_fp16_blocks_first", 402, 20000, 8, 128, 16, 4, 4, 16, 16, np.float32, False, True),
+    # staged rows: truncated streams (groups reaching the read limit take global loads) and
+    # out-of-range block ids, at symbol widths 5 / 3 and 4 / 2
+    cachegen_cache_case("cg_staged_truncated", 403, 3001, 4, 64, 16, 5, 3, 32, 8, np.float16, True, False,
+                        trunc=(101, 7)),
+    cachegen_cache_case("cg_staged_bad_ids", 404, 2050, 2, 128, 16, 4, 2, 16, 4, np.float32, False, True, bad=True),
     kivi_case("kivi_c2_layer_b2", 403, 32768, 128, 8, 128, 16, 2, 64, np.float16, True, False, spare_blocks=40),
     kivi_case("kivi_b4_d64_ragged", 404, 9999, 32, 4, 64, 32, 4, 32, np.float16, False, True),
     kivi_case("kivi_b3_d256", 405, 5000, 0, 2, 256, 16, 3, 128, np.float32, True, False),
