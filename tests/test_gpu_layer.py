@@ -219,3 +219,86 @@ def test_prefix_restore_checks_its_token_count(cuda):
     for bad in (0, T + 1):
         with pytest.raises(RuntimeError, match="restore_tokens"):
             restore_layer(packed, fmt, d, ids, num_tokens=bad)
+
+
+def _request_rows(cache, ids, T):
+    """A request's token rows [2, T, H, D] gathered from a paged cache (KV-first)."""
+    bs = cache.shape[2]
+    t = torch.arange(T, device=cache.device)
+    return cache[:, ids[t // bs], t % bs]
+
+
+def test_c3_layer_in_its_shared_pool_matches_oracle(oracle, cuda):
+    """One C3 layer at full size: the 16 ragged requests (T ~ U[4096, 65536]) share one pool
+    sized for 120 GB over 32 layers, through interleaved block tables. Requests with the same
+    token count are packed in one batched launch, as bench.py does. The oracle checks the
+    packed bytes of the shortest and the longest request; restoring every request into a
+    fresh pool reproduces each request's rows and writes no other block."""
+    from origami_b200.layer import alloc_jobs_packed, job_stride, pack_layers, restore_layers
+
+    cfg = workloads.c3_config()
+    tokens, bs, H, D = list(cfg.tokens), cfg.block_size, cfg.heads, cfg.head_dim
+    NB = workloads.c3_pool_blocks(cfg)
+    tables = [t.to(cuda) for t in workloads.interleaved_block_tables(tokens, bs, NB, workloads.SEED + 5)]
+    g = torch.Generator(device=cuda).manual_seed(11)
+    pool = torch.randint(-32768, 32767, (2, NB, bs, H, D), generator=g, device=cuda, dtype=torch.int16).view(cfg.dtype)
+    for r, T in enumerate(tokens):
+        kv = workloads.kv_values(T, H, D, cfg.dtype, seed=workloads.SEED + r, v_std=cfg.v_std, device=cuda)
+        workloads.scatter_into_cache(pool, kv, tables[r])
+    groups: dict[int, list[int]] = {}
+    for r, T in enumerate(tokens):
+        groups.setdefault(T, []).append(r)
+    packed = {}
+    fresh = torch.zeros_like(pool)
+    for T, reqs in groups.items():
+        fmt = LayerFormat(T, H, D, BYTE_PLANES)
+        arena = alloc_jobs_packed(fmt, len(reqs), cuda)
+        pack_layers([pool] * len(reqs), [tables[r] for r in reqs], fmt, arena)
+        stride = job_stride(fmt)
+        for j, r in enumerate(reqs):
+            packed[r] = (fmt, arena[j * stride:j * stride + fmt.packed_bytes])
+        restore_layers(arena, fmt, [fresh] * len(reqs), [tables[r] for r in reqs])
+    for r in (int(np.argmin(tokens)), int(np.argmax(tokens))):
+        T = tokens[r]
+        fmt, got = packed[r]
+        nb = (T + bs - 1) // bs
+        compact = pool[:, tables[r][:nb]]  # the request's blocks, in table order
+        want, _ = oracle.pack_layer(u16(compact.cpu()), 0, np.arange(nb, dtype=np.int64), T, BYTE_PLANES.shifts,
+                                    BYTE_PLANES.bits, fmt.specs)
+        np.testing.assert_array_equal(got.cpu().numpy(), want, err_msg=f"request {r} (T={T})")
+    used = torch.zeros(NB, dtype=torch.bool, device=cuda)
+    for r, T in enumerate(tokens):
+        assert torch.equal(_request_rows(fresh, tables[r], T).view(torch.int16),
+                           _request_rows(pool, tables[r], T).view(torch.int16)), f"request {r}"
+        used[tables[r]] = True
+    assert not bool(fresh[:, ~used].view(torch.int16).any())
+
+
+def test_c5_save_layer_batched_matches_oracle(oracle, cuda):
+    """One C5 save layer at full size: 64 requests x 8192 tokens (Qwen2-7B KV: 4 heads,
+    D 128, bf16, block 16) packed in one batched launch; the oracle checks jobs 0, 31 and
+    63, and restoring every job gives the requests' rows back."""
+    from origami_b200.layer import alloc_jobs_packed, job_stride, pack_layers, restore_layers
+
+    cfg = workloads.C5
+    R, T, bs, H, D = len(cfg.tokens), cfg.tokens[0], cfg.block_size, cfg.heads, cfg.head_dim
+    nb = T // bs
+    pool = workloads.permuted_block_table(nb * R, nb * R, workloads.SEED + 4)
+    tables = [pool[r * nb:(r + 1) * nb].to(cuda) for r in range(R)]
+    cache = torch.empty((2, nb * R, bs, H, D), dtype=cfg.dtype, device=cuda)
+    for r in range(R):
+        kv = workloads.kv_values(T, H, D, cfg.dtype, seed=workloads.SEED + r, v_std=cfg.v_std, device=cuda)
+        workloads.scatter_into_cache(cache, kv, tables[r])
+    fmt = LayerFormat(T, H, D, BYTE_PLANES)
+    arena = alloc_jobs_packed(fmt, R, cuda)
+    pack_layers([cache] * R, tables, fmt, arena)
+    stride = job_stride(fmt)
+    for r in (0, R // 2 - 1, R - 1):
+        compact = cache[:, tables[r]]
+        want, _ = oracle.pack_layer(u16(compact.cpu()), 0, np.arange(nb, dtype=np.int64), T, BYTE_PLANES.shifts,
+                                    BYTE_PLANES.bits, fmt.specs)
+        np.testing.assert_array_equal(arena[r * stride:r * stride + fmt.packed_bytes].cpu().numpy(), want,
+                                      err_msg=f"job {r}")
+    fresh = torch.zeros_like(cache)
+    restore_layers(arena, fmt, [fresh] * R, tables)
+    assert torch.equal(fresh.view(torch.int16), cache.view(torch.int16))
