@@ -283,13 +283,37 @@ __device__ __forceinline__ uint64_t field_from_smem(const uint8_t* p) {
   return (static_cast<uint64_t>(w1 >> sh) << 32) | __funnelshift_r(w0, w1, sh);
 }
 
-// One staged row of BITS-bit symbols: lane l's vectors l, l + 32, ... from shared memory.
-template <int BITS, typename OUT>
-__device__ __forceinline__ void cg_row_smem(const uint8_t* row, int nvec, uint32_t lut, OUT* dst, int lane) {
+// Eight BITS-bit symbols -> eight output elements by warp shuffle within segments of
+// 2^BITS lanes: lane l holds the finished element for symbol value l mod 2^BITS, and the
+// shuffle takes its source lane modulo the segment width, so a symbol's field needs a shift
+// but no mask. All 32 lanes must execute it.
+template <int BITS>
+__device__ __forceinline__ uint4 lookup8_seg(uint32_t lut, uint64_t field) {
+  constexpr int W = 1 << BITS;
+  const uint32_t w[2] = {static_cast<uint32_t>(field), static_cast<uint32_t>(field >> (4 * BITS))};
+  uint32_t o[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t x = w[j >> 1];
+    const int k = 2 * (j & 1);
+    const uint32_t e0 = __shfl_sync(0xFFFFFFFFu, lut, static_cast<int>(x >> (k * BITS)), W);
+    const uint32_t e1 = __shfl_sync(0xFFFFFFFFu, lut, static_cast<int>(x >> ((k + 1) * BITS)), W);
+    o[j] = __byte_perm(e0, e1, 0x5410);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// One row of BITS-bit symbols: lane l's vectors l, l + 32, ... from the staged row (STAGED)
+// or, for a group that reaches the stream's read limit, from global memory with the
+// reference's bounds rule.
+template <int BITS, bool STAGED, typename OUT>
+__device__ __forceinline__ void cg_row_seg(const uint8_t* row, const uint8_t* gs, int64_t nb, int64_t k0, int nvec,
+                                           uint32_t lut, OUT* dst, int lane) {
   for (int v0 = 0; v0 < nvec; v0 += 32) {
     const int v = v0 + lane;
-    const uint64_t field = v < nvec ? field_from_smem<BITS>(row + v * BITS) : 0;
-    const uint4 out = lookup8_shfl(lut, field, BITS);
+    uint64_t field = 0;
+    if (v < nvec) field = STAGED ? field_from_smem<BITS>(row + v * BITS) : symbols8_raw(gs, nb, k0 + v, BITS);
+    const uint4 out = lookup8_seg<BITS>(lut, field);
     if (v < nvec) st_global_cs16(dst + 8 * v, out);
   }
 }
@@ -382,29 +406,26 @@ __global__ void __launch_bounds__(kThreads, 4) cachegen_staged(const __grid_cons
         const int64_t bi = static_cast<int32_t>(t) / static_cast<int32_t>(a.block_size);
         OUT* dst = reinterpret_cast<OUT*>(a.cache) + kv * a.kv_stride + blk * a.block_stride +
                    (t - bi * a.block_size) * a.token_stride;
-        const uint32_t lut = out_bits<OUT>(table[kv][lane] * gmax[s][rr]);
-        if (off_cur >= 0) {
-          const uint8_t* row = cg_stage + s * stage_bytes + off_cur + rr * a.nvec * bits;
-          switch (bits) {  // warp-uniform
-            case 5: cg_row_smem<5, OUT>(row, a.nvec, lut, dst, lane); break;
-            case 4: cg_row_smem<4, OUT>(row, a.nvec, lut, dst, lane); break;
-            case 3: cg_row_smem<3, OUT>(row, a.nvec, lut, dst, lane); break;
-            case 2: cg_row_smem<2, OUT>(row, a.nvec, lut, dst, lane); break;
-            default: cg_row_smem<1, OUT>(row, a.nvec, lut, dst, lane); break;
-          }
+        // lane l: the element for symbol value l mod 2^bits (segmented shuffles)
+        const uint32_t lut = out_bits<OUT>(table[kv][lane & ((1 << bits) - 1)] * gmax[s][rr]);
+        const uint8_t* row = off_cur >= 0 ? cg_stage + s * stage_bytes + off_cur + rr * a.nvec * bits : nullptr;
+        const uint8_t* gs = a.stream[kv];
+        const int64_t nb = a.stream_bytes[kv];
+        const int64_t k0 = t * a.nvec;
+#define ORIGAMI_CG_ROW(ST)                                                          \
+  switch (bits) { /* warp-uniform */                                                \
+    case 5: cg_row_seg<5, ST, OUT>(row, gs, nb, k0, a.nvec, lut, dst, lane); break;   \
+    case 4: cg_row_seg<4, ST, OUT>(row, gs, nb, k0, a.nvec, lut, dst, lane); break;   \
+    case 3: cg_row_seg<3, ST, OUT>(row, gs, nb, k0, a.nvec, lut, dst, lane); break;   \
+    case 2: cg_row_seg<2, ST, OUT>(row, gs, nb, k0, a.nvec, lut, dst, lane); break;   \
+    default: cg_row_seg<1, ST, OUT>(row, gs, nb, k0, a.nvec, lut, dst, lane); break;  \
+  }
+        if (row) {
+          ORIGAMI_CG_ROW(true)
         } else {
-          // the group reaches the stream's read limit: global loads with the bounds rule
-          const uint8_t* gs = a.stream[kv];
-          const int64_t nb = a.stream_bytes[kv];
-          const int64_t k0 = t * a.nvec;
-          switch (bits) {
-            case 5: cg_row_shfl<5, OUT>(gs, nb, k0, a.nvec, lut, dst, lane); break;
-            case 4: cg_row_shfl<4, OUT>(gs, nb, k0, a.nvec, lut, dst, lane); break;
-            case 3: cg_row_shfl<3, OUT>(gs, nb, k0, a.nvec, lut, dst, lane); break;
-            case 2: cg_row_shfl<2, OUT>(gs, nb, k0, a.nvec, lut, dst, lane); break;
-            default: cg_row_shfl<1, OUT>(gs, nb, k0, a.nvec, lut, dst, lane); break;
-          }
+          ORIGAMI_CG_ROW(false)
         }
+#undef ORIGAMI_CG_ROW
       }
     }
     if (!has_next) break;
