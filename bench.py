@@ -584,6 +584,7 @@ def run_origami(args, rank, world, local):
         result["bundle_e2e"] = bundle_info
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"], result["cpu_baselines"] = cpu_baseline(args, wl)
+        result["host"] = host_cpu()
     if rank == 0:
         print(json.dumps(with_nominal(result)), flush=True)
     return 0 if ok else 1
@@ -963,6 +964,20 @@ def run_pipeline_c4(args, device, world):
         "bytes_per_layer": R * fmt.packed_bytes,
         "ok": ok,
     }
+
+
+def host_cpu() -> dict:
+    """The host the CPU baselines ran on: threads, CPU model and NUMA nodes."""
+    model = None
+    try:
+        for ln in open("/proc/cpuinfo"):
+            if ln.startswith("model name"):
+                model = ln.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    nodes = len([n for n in Path("/sys/devices/system/node").glob("node[0-9]*")]) or None
+    return {"nproc": os.cpu_count(), "cpu_model": model, "numa_nodes": nodes}
 
 
 def cpu_baseline(args, wl):
