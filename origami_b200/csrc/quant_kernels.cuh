@@ -925,10 +925,13 @@ struct Kivi2Geo {
   static constexpr int rows_bytes = TT * row_bytes + (TT / 8) * 16;
   static constexpr int runs_off = rows_bytes;
   static constexpr int bit0_off = runs_off + D * rs;
-  static constexpr int meta_off = bit0_off + D * 4;
-  // (scale, zero): values as [group slot][token], keys as [group slot][channel]
-  static constexpr int meta_elems = kMetaSlots * (TT > D ? TT : D);
-  static constexpr int smem_bytes = meta_off + 2 * meta_elems * static_cast<int>(sizeof(META));
+  static constexpr int lut_off = bit0_off + D * 4;
+  // finished 4-entry tables fma(s, scale, zero), s = 0..3, of up to kSlots groups: values
+  // as [group slot][token % 8][token / 8] (the threads of a token octet read consecutive
+  // entries), keys as [group slot][channel]
+  static constexpr int kSlots = 3;
+  static constexpr int lut_entries = kSlots * (TT > D ? TT : D);
+  static constexpr int smem_bytes = lut_off + lut_entries * 8;
   // 5 CTAs an SM where their shared memory fits (1 KB reserved per CTA of 228 KB), else 4
   static constexpr int min_ctas = 5 * (smem_bytes + 1024) <= 228 * 1024 ? 5 : 4;
   static_assert(TT <= kThreads, "one token row per thread");
@@ -948,8 +951,7 @@ __global__ void __launch_bounds__(kThreads, Kivi2Geo<D, META>::min_ctas) kivi2_t
   uint8_t* rows_sm = kivi2_smem;
   uint8_t* runs = kivi2_smem + G::runs_off;
   int32_t* bit0 = reinterpret_cast<int32_t*>(kivi2_smem + G::bit0_off);
-  META* msc = reinterpret_cast<META*>(kivi2_smem + G::meta_off);
-  META* mze = msc + G::meta_elems;
+  uint2* lut = reinterpret_cast<uint2*>(kivi2_smem + G::lut_off);
   const int tid = threadIdx.x;
   const int64_t C = static_cast<int64_t>(a.H) * D;
   const int ao = tid % G::A;
@@ -1013,9 +1015,9 @@ __global__ void __launch_bounds__(kThreads, Kivi2Geo<D, META>::min_ctas) kivi2_t
       }
       asm volatile("cp.async.commit_group;\n" ::: "memory");
     }
-    // this tile's scale / zero in shared memory when they fit in kMetaSlots value groups
-    // ([group slot][token]) or key groups ([group slot][channel]); otherwise the
-    // dequantization reads them from global memory
+    // this tile's tables in shared memory when they fit in kSlots value groups or key
+    // groups (each thread loads one (scale, zero) pair and writes its finished table);
+    // otherwise the dequantization builds them from global memory
     bool staged = false;
     int mbase = 0;  // first staged value group / key group
     if (nbody > 0) {
@@ -1024,27 +1026,25 @@ __global__ void __launch_bounds__(kThreads, Kivi2Geo<D, META>::min_ctas) kivi2_t
       if (kv) {
         mbase = (h * D) >> gs;
         const int ng = ((h * D + D - 1) >> gs) - mbase + 1;
-        if (ng <= kMetaSlots) {
+        if (ng <= G::kSlots) {
           staged = true;
           for (int e = tid; e < ng * G::TT; e += kThreads) {
             const int g = e / G::TT;
             const int rr = e % G::TT;
             if (rr < nbody) {
               const int64_t idx = static_cast<int64_t>(tb0 - sink + rr) * a.value_groups + mbase + g;
-              msc[e] = sc[idx];
-              mze[e] = ze[idx];
+              lut[(g * 8 + (rr & 7)) * G::A + (rr >> 3)] = lut4<OUT>(to_f32(sc[idx]), to_f32(ze[idx]));
             }
           }
         }
       } else {
         mbase = (tb0 - sink) >> gs;
         const int nkg = ((tb1 - 1 - sink) >> gs) - mbase + 1;
-        if (nkg <= kMetaSlots) {
+        if (nkg <= G::kSlots) {
           staged = true;
           for (int e = tid; e < nkg * D; e += kThreads) {
             const int64_t idx = static_cast<int64_t>(mbase + e / D) * C + h * D + (e % D);
-            msc[e] = sc[idx];
-            mze[e] = ze[idx];
+            lut[e] = lut4<OUT>(to_f32(sc[idx]), to_f32(ze[idx]));
           }
         }
       }
@@ -1089,24 +1089,18 @@ __global__ void __launch_bounds__(kThreads, Kivi2Geo<D, META>::min_ctas) kivi2_t
         if (kv) {
           // values: one (scale, zero) per token and channel group, one table per token
           const int g = ch0 >> gs;
-          VecOf<META> vs, vz;
-          if (staged) {  // tokens k0 .. k0 + 7 of group g (k0 % 8 == 0): one vector each
-            const int base = (g - mbase) * G::TT + k0;
-            vs = *reinterpret_cast<const VecOf<META>*>(msc + base);
-            vz = *reinterpret_cast<const VecOf<META>*>(mze + base);
-          } else {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const int64_t idx = static_cast<int64_t>(min(bq + i, static_cast<int>(a.body_tokens) - 1)) *
-                                      a.value_groups + g;
-              vs.v[i] = sc[idx];
-              vz.v[i] = ze[idx];
-            }
-          }
+          // body token k0 + i of group g (k0 % 8 == 0): octet k0 / 8, entry i
+          const uint2* lp = lut + ((g - mbase) * 8) * G::A + (k0 >> 3);
+          auto table = [&](int i) -> uint2 {
+            if (staged) return lp[i * G::A];
+            const int64_t idx =
+                static_cast<int64_t>(min(bq + i, static_cast<int>(a.body_tokens) - 1)) * a.value_groups + g;
+            return lut4<OUT>(to_f32(sc[idx]), to_f32(ze[idx]));
+          };
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            const uint2 tl = lut4<OUT>(to_f32(vs.v[k]), to_f32(vz.v[k]));
-            const uint2 th = lut4<OUT>(to_f32(vs.v[k + 4]), to_f32(vz.v[k + 4]));
+            const uint2 tl = table(k);
+            const uint2 th = table(k + 4);
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
               const uint32_t y = kivi2_selectors(w2[c], k);
@@ -1117,22 +1111,20 @@ __global__ void __launch_bounds__(kThreads, Kivi2Geo<D, META>::min_ctas) kivi2_t
         } else {
           // keys: one (scale, zero) per channel and token group, one table per channel;
           // channel A's table gives the low half of a word, channel B's the high half
-          VecOf<META> vs, vz;
+          uint2 t[8];
           if (staged) {
-            const int base = ((bq >> gs) - mbase) * D + 8 * o;
-            vs = *reinterpret_cast<const VecOf<META>*>(msc + base);
-            vz = *reinterpret_cast<const VecOf<META>*>(mze + base);
+            const uint4* lp = reinterpret_cast<const uint4*>(lut + ((bq >> gs) - mbase) * D + 8 * o);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const uint4 v = lp[q];
+              t[2 * q] = make_uint2(v.x, v.y);
+              t[2 * q + 1] = make_uint2(v.z, v.w);
+            }
           } else {
             const int64_t base = static_cast<int64_t>(bq >> gs) * C + ch0;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              vs.v[j] = sc[base + j];
-              vz.v[j] = ze[base + j];
-            }
+            for (int j = 0; j < 8; ++j) t[j] = lut4<OUT>(to_f32(sc[base + j]), to_f32(ze[base + j]));
           }
-          uint2 t[8];
-#pragma unroll
-          for (int j = 0; j < 8; ++j) t[j] = lut4<OUT>(to_f32(vs.v[j]), to_f32(vz.v[j]));
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
 #pragma unroll
