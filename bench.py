@@ -511,6 +511,7 @@ def run_origami(args, rank, world, local):
         pipeline_info = run_pipeline_c4(args, device, world)
         ok = ok and pipeline_info.pop("ok")
 
+    barrier(world)  # every rank probes at once: the share of shared host links its copies see
     pcie = measure_pcie(device)
     if pipeline_info is not None:
         pipeline_info["pcie_h2d_frac"] = round(pipeline_info["pcie_h2d_gbs"] / pcie["h2d_gbs"], 3)
@@ -593,7 +594,8 @@ def run_origami(args, rank, world, local):
 def measure_pcie(device) -> dict:
     """Pinned host <-> device copy peak of this box, in this run: 256 MiB cudaMemcpyAsync
     each way on one stream, best of 10 after 3 warm-ups (the roofline of the e2e and
-    pipeline numbers)."""
+    pipeline numbers). With several ranks the caller starts every rank's probe together,
+    so the figure is a rank's share of host links the ranks share, as in their e2e copies."""
     import torch
 
     n = 256 << 20
