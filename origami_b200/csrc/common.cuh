@@ -203,25 +203,6 @@ __device__ __forceinline__ void words5(const uint32_t* src, int q, uint32_t (&s)
   }
 }
 
-// Spread 8 consecutive `bits`-wide symbols of a 64-bit window into 8 bytes.
-template <int BITS>
-__device__ __forceinline__ void spread8_ct(uint32_t v0, uint32_t v1, uint32_t& lo, uint32_t& hi) {
-  if constexpr (BITS == 8) {
-    lo = v0;
-    hi = v1;
-  } else {
-    const uint64_t v = (static_cast<uint64_t>(v1) << 32) | v0;
-    constexpr uint32_t m = (1u << BITS) - 1u;
-    lo = static_cast<uint32_t>(v & m) | (static_cast<uint32_t>((v >> BITS) & m) << 8) |
-         (static_cast<uint32_t>((v >> (2 * BITS)) & m) << 16) |
-         (static_cast<uint32_t>((v >> (3 * BITS)) & m) << 24);
-    hi = static_cast<uint32_t>((v >> (4 * BITS)) & m) |
-         (static_cast<uint32_t>((v >> (5 * BITS)) & m) << 8) |
-         (static_cast<uint32_t>((v >> (6 * BITS)) & m) << 16) |
-         (static_cast<uint32_t>((v >> (7 * BITS)) & m) << 24);
-  }
-}
-
 __device__ __forceinline__ void spread8_rt(uint32_t v0, uint32_t v1, int bits, uint32_t& lo,
                                            uint32_t& hi) {
   if (bits == 8) {

@@ -102,13 +102,6 @@ __device__ __forceinline__ uint64_t symbols8_raw(const uint8_t* s, int64_t nbyte
   return v;
 }
 
-// Symbols 8k .. 8k+7 as eight bytes (lo: symbols 0..3, hi: 4..7).
-__device__ __forceinline__ void symbols8(const uint8_t* s, int64_t nbytes, int64_t k, int bits, uint32_t& lo,
-                                         uint32_t& hi) {
-  const uint64_t v = symbols8_raw(s, nbytes, k, bits);
-  spread8_rt(static_cast<uint32_t>(v), static_cast<uint32_t>(v >> 32), bits, lo, hi);
-}
-
 // Eight b-bit symbols of a 64-bit field (symbol k at bits [k*b, (k+1)*b)) -> eight
 // dequantized elements q[s] * m, packed as 16 bytes. Symbols 0..3 come from the low word,
 // 4..7 from the field shifted by 4*b; each is one shift and one mask from its table index.
@@ -890,7 +883,6 @@ __global__ void __launch_bounds__(kThreads) kivi_to_cache(const __grid_constant_
     __syncthreads();
   }
 }
-
 
 // ---------------------------------------------------------------------------------------
 // 2-bit KIVI (the reference's default width) -> paged cache

@@ -406,13 +406,6 @@ __device__ __forceinline__ void cp_async16_zfill(void* smem_dst, const void* gme
                : "memory");
 }
 
-// 1-D bulk copy shared -> global (16-byte aligned addresses, size a multiple of 16).
-__device__ __forceinline__ void bulk_store(void* gmem_dst, const void* smem_src, uint32_t bytes) {
-  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;\n" ::"l"(gmem_dst), "r"(smem_u32(smem_src)),
-               "r"(bytes)
-               : "memory");
-}
-
 __device__ __forceinline__ uint32_t word_of(const uint4& v, int i) {
   return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
 }
